@@ -1,0 +1,569 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention path (one JSON line on stdout, rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl mako|reference]
+
+Workloads (synthetic seeded data -- no dataset is involved):
+  decode         configs[1]: GQA decode fp16, batch 8, 32 q / 8 kv heads, D 128, KV lengths U[16384, 32768]  (default)
+  prefill        configs[2]: causal GQA prefill bf16, batch 2 (folded into heads), 32 / 8 heads, D 128, S 8192
+  sparse         configs[3]: block-sparse bf16, 24 heads, D 128, S 16384, 64x64 blocks, diagonal + 15% per row
+  bidir          configs[4]: bidirectional bf16, 24 heads, D 128, N 75600, RMS-normalised q and k
+  prefill_small  configs[0]: causal GQA prefill fp16, 16 / 8 heads, D 128, S 512
+A step is one call of the public C ABI (include/mako_attn.h) over one batch held in HBM; `value` is device time
+(CUDA events on the launching stream, L2 flushed between steps, max over ranks); `e2e` is the same metric with the
+step's inputs copied from pinned host memory and its output read back inside the timed region.  With N > 1 the
+decode / prefill_small / sparse / prefill workloads run one replica per GPU (weak scaling).
+
+--impl reference times the reference's scalar attention restated on the CPU (oracle/, all host threads) on a
+bounded sample of the same workload: the reference itself is Metal-only and cannot run here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(ROOT, "mako-common_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+UINT32_MAX = 0xFFFFFFFF
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def round_up(x, m):
+    return (x + m - 1) // m * m
+
+
+# ---- workloads ------------------------------------------------------------------------------------------------------
+
+class Workload:
+    """Holds device inputs, knows its algorithmic work, runs one step through the C ABI."""
+    name = ""
+    metric = ""
+    unit = ""
+    bound = "tensor"
+    dtype = "bf16"
+
+    def work(self) -> float:  # algorithmic units (bytes or FLOP) per step
+        raise NotImplementedError
+
+    def to_metric(self, units_per_s: float) -> float:
+        return units_per_s / (1e9 if self.bound == "hbm" else 1e12)
+
+
+DEVICE = "cuda"  # "cpu" for the reference arm, which needs no GPU
+
+
+def gen(shape, dtype, seed, scale=1.0, rms_norm=False):
+    """Seeded N(0, 1) from torch's CPU generator (the same values for both arms), moved to DEVICE."""
+    import torch
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    x = torch.randn(shape, generator=g, dtype=torch.float32)
+    if rms_norm:
+        x = x * torch.rsqrt((x * x).mean(dim=-1, keepdim=True))
+    return (x * scale).to(dtype).to(DEVICE)
+
+
+class Decode(Workload):
+    name, metric, unit, bound, dtype = "decode", "decode KV-read GB/s (GQA, split-KV)", "GB/s", "hbm", "fp16"
+
+    def __init__(self, seed=0):
+        import numpy as np
+        import torch
+        self.B, self.H, self.KV, self.D = 8, 32, 8, 128
+        rng = np.random.default_rng(seed)
+        self.lens = rng.integers(16384, 32768 + 1, size=self.B).astype(np.int32)
+        self.S = int(round_up(int(self.lens.max()), 64))
+        self.q = gen((self.B, self.H, self.D), torch.float16, seed + 1)
+        self.k = gen((self.B, self.KV, self.S, self.D), torch.float16, seed + 2)
+        self.v = gen((self.B, self.KV, self.S, self.D), torch.float16, seed + 3)
+        for b in range(self.B):  # rows past a sequence's length are zero, as a cache leaves them
+            self.k[b, :, self.lens[b]:] = 0
+            self.v[b, :, self.lens[b]:] = 0
+        self.kv_len = torch.from_numpy(self.lens).to(DEVICE)
+        self.o = torch.empty((self.B, self.H * self.D), dtype=torch.float32, device=DEVICE)
+        self.inputs = [self.q, self.k, self.v]
+        self.outputs = [self.o]
+        self.launches_per_step = 2
+        self.config = {"workload": "decode (configs[1])", "batch": self.B, "q_heads": self.H, "kv_heads": self.KV,
+                       "head_dim": self.D, "kv_len": [int(x) for x in self.lens], "kv_len_seed": seed,
+                       "cache_rows": self.S, "dtype": "fp16", "l2": "flushed between steps (256 MB write)"}
+
+    def work(self):
+        return float(sum(2 * self.KV * int(L) * self.D * 2 for L in self.lens) + self.B * self.H * self.D * (2 + 4))
+
+    def step(self, ctx):
+        ctx.attention_decode(self.q, self.k, self.v, self.o, self.kv_len, int(self.lens.max()), self.H, self.KV,
+                             self.D, self.S)
+
+    # CPU sample: the whole workload (the oracle decode is a few seconds on a host)
+    def cpu_sample(self, O, threads, frac=1.0):
+        import numpy as np
+        nb = max(1, int(round(self.B * frac)))
+        q = self.q[:nb].cpu().view(torch_int16()).numpy().view(np.uint16)
+        k = self.k[:nb].cpu().view(torch_int16()).numpy().view(np.uint16)
+        v = self.v[:nb].cpu().view(torch_int16()).numpy().view(np.uint16)
+        lens = self.lens[:nb]
+
+        def run():
+            return O.decode(0, q, k, v, lens, self.H, self.KV, self.D, self.S, nthreads=threads)
+        work = float(sum(2 * self.KV * int(L) * self.D * 2 for L in lens) + nb * self.H * self.D * 6)
+        return run, work, f"batch {nb} of {self.B} (all heads, full lengths)"
+
+    def check(self, O):
+        import numpy as np
+        b = [0, self.B - 1]
+        got = self.o[b].cpu().numpy()
+        q = self.q[b].cpu().view(torch_int16()).numpy().view(np.uint16)
+        k = self.k[b].cpu().view(torch_int16()).numpy().view(np.uint16)
+        v = self.v[b].cpu().view(torch_int16()).numpy().view(np.uint16)
+        want = O.decode(0, q, k, v, self.lens[b], self.H, self.KV, self.D, self.S)
+        return got, want, "sequences 0 and 7"
+
+
+class Prefill(Workload):
+    """Dense masked prefill; batch folded into heads (head h of batch b is head b * H + h)."""
+    bound = "tensor"
+
+    def __init__(self, name, metric, B, H, KV, D, S, dtype, scale, block, seed, rms_qk=False, cfg=""):
+        import torch
+        self.name, self.metric, self.unit = name, metric, "TFLOP/s"
+        self.B, self.H, self.KV, self.D, self.S, self.block = B, H, KV, D, S, block
+        self.tdtype = torch.bfloat16 if dtype == "bf16" else torch.float16
+        self.dtype = dtype
+        self.heads, self.kv_heads = B * H, B * KV
+        self.q_pad, self.k_pad = round_up(S, 64), round_up(S, 128)
+        self.q = torch.zeros((self.heads, self.q_pad, D), dtype=self.tdtype, device=DEVICE)
+        self.k = torch.zeros((self.kv_heads, self.k_pad, D), dtype=self.tdtype, device=DEVICE)
+        self.v = torch.zeros_like(self.k)
+        self.q[:, :S] = gen((self.heads, S, D), self.tdtype, seed + 1, scale, rms_qk)
+        self.k[:, :S] = gen((self.kv_heads, S, D), self.tdtype, seed + 2, scale, rms_qk)
+        self.v[:, :S] = gen((self.kv_heads, S, D), self.tdtype, seed + 3, scale)
+        self.o = torch.empty((S, self.heads * D), dtype=torch.float32, device=DEVICE)
+        self.inputs, self.outputs = [self.q, self.k, self.v], [self.o]
+        self.launches_per_step = 1
+        self.config = {"workload": cfg, "batch": B, "q_heads": H, "kv_heads": KV, "head_dim": D, "seq_len": S,
+                       "mask": "causal" if block == UINT32_MAX else ("bidirectional" if block == 0 else f"block {block}"),
+                       "dtype": dtype, "input_scale": scale, "rms_norm_qk": rms_qk, "seed": seed,
+                       "l2": "flushed between steps (256 MB write)"}
+
+    def visible(self, i):
+        return self.S if (i >= self.block) else min(self.S, i + 1)
+
+    def work(self):
+        if self.block == UINT32_MAX:
+            return 4.0 * self.D * self.heads * self.S * (self.S + 1) / 2
+        if self.block == 0:
+            return 4.0 * self.D * self.heads * self.S * self.S
+        return float(sum(4 * self.D * self.heads * self.visible(i) for i in range(self.S)))
+
+    def step(self, ctx):
+        ctx.attention(self.q, self.k, self.v, self.o, self.S, self.q_pad, self.S, self.k_pad, self.heads,
+                      self.kv_heads, 0, self.block, self.D)
+
+    def sample_rows(self, n):
+        import numpy as np
+        return np.unique(np.linspace(0, self.S - 1, n).astype(np.uint32))
+
+    def _bits(self):
+        import numpy as np
+        code = 1 if self.dtype == "bf16" else 0
+        f = lambda t: t.cpu().view(torch_int16()).numpy().view(np.uint16)  # noqa: E731
+        return code, f(self.q), f(self.k), f(self.v)
+
+    def cpu_sample(self, O, threads, target_s=10.0):
+        code, q, k, v = self._bits()
+        # rows per second on this host, from a small probe, then a sample sized for ~target_s
+        probe = self.sample_rows(8)
+        t0 = time.perf_counter()
+        O.attention(code, q, k, v, self.S, self.q_pad, self.S, self.k_pad, self.heads, self.kv_heads, 0, self.block,
+                    self.D, rows=probe, nthreads=threads)
+        dt = max(time.perf_counter() - t0, 1e-3)
+        n = int(min(self.S, max(8, len(probe) * target_s / dt)))
+        rows = self.sample_rows(n)
+        work = float(sum(4 * self.D * self.heads * self.visible(int(i)) for i in rows))
+
+        def run():
+            return O.attention(code, q, k, v, self.S, self.q_pad, self.S, self.k_pad, self.heads, self.kv_heads, 0,
+                               self.block, self.D, rows=rows, nthreads=threads)
+        return run, work, f"{len(rows)} of {self.S} query rows (evenly spaced), all {self.heads} heads; " \
+                          "rate extrapolated linearly in rows"
+
+    def check(self, O):
+        import numpy as np
+        code, q, k, v = self._bits()
+        rows = self.sample_rows(24)
+        want = O.attention(code, q, k, v, self.S, self.q_pad, self.S, self.k_pad, self.heads, self.kv_heads, 0,
+                           self.block, self.D, rows=rows)
+        return self.o.cpu().numpy()[rows], want[rows], f"{len(rows)} query rows x all heads"
+
+
+class Sparse(Workload):
+    name, metric, unit, bound, dtype = "sparse", "block-sparse attention TFLOP/s on kept blocks", "TFLOP/s", \
+        "tensor", "bf16"
+
+    def __init__(self, seed=0):
+        import torch
+        import attn_cases as C
+        self.H, self.D, self.S, self.frac = 24, 128, 16384, 0.15
+        self.nb = self.S // 64
+        lists, counts = C.block_lists(seed, self.H, self.nb, self.frac)
+        self.lists_np, self.counts_np = lists, counts
+        self.lists, self.counts = torch.from_numpy(lists).to(DEVICE), torch.from_numpy(counts).to(DEVICE)
+        self.q = gen((self.H, self.S, self.D), torch.bfloat16, seed + 1)
+        self.k = gen((self.H, self.S, self.D), torch.bfloat16, seed + 2)
+        self.v = gen((self.H, self.S, self.D), torch.bfloat16, seed + 3)
+        self.o = torch.empty((self.S, self.H * self.D), dtype=torch.float32, device=DEVICE)
+        self.inputs, self.outputs = [self.q, self.k, self.v], [self.o]
+        self.launches_per_step = 1
+        self.config = {"workload": "sparse (configs[3])", "heads": self.H, "head_dim": self.D, "seq_len": self.S,
+                       "block": 64, "kept_per_query_block": int(lists.shape[-1]), "keep_fraction": self.frac,
+                       "mask": "int32 sorted kept-block lists + counts", "dtype": "bf16", "seed": seed,
+                       "l2": "flushed between steps (256 MB write)"}
+
+    def work(self):
+        return float(int(self.counts_np.sum()) * 4 * 64 * 64 * self.D)
+
+    def step(self, ctx):
+        ctx.attention_block_sparse(self.q, self.k, self.v, self.o, self.S, self.H, self.H, self.lists, self.counts)
+
+    def _args(self, O):
+        import numpy as np
+        f = lambda t: t.cpu().view(torch_int16()).numpy().view(np.uint16)  # noqa: E731
+        return (1, f(self.q), f(self.k), f(self.v), self.S, self.S, self.S, self.S, self.H, self.H, self.H * self.D,
+                self.nb, self.lists_np.shape[-1], self.S, self.S, self.lists_np.astype(np.uint16),
+                self.counts_np.astype(np.uint16), np.ones(self.S, np.uint8), np.arange(self.S, dtype=np.int32))
+
+    def cpu_sample(self, O, threads, target_s=10.0):
+        import numpy as np
+        args = self._args(O)
+        out = np.zeros((self.S, self.H * self.D), np.float32)
+        probe = np.arange(0, self.S, self.S // 8, dtype=np.uint32)
+        t0 = time.perf_counter()
+        O.attention_sparse(*args, out=out, rows=probe, nthreads=threads)
+        dt = max(time.perf_counter() - t0, 1e-3)
+        n = int(min(self.S, max(8, len(probe) * target_s / dt)))
+        rows = np.unique(np.linspace(0, self.S - 1, n).astype(np.uint32))
+        kept = self.counts_np.sum(axis=0)  # per query block, over heads
+        work = float(sum(int(kept[r // 64]) * 64 * 4 * self.D for r in rows))
+
+        def run():
+            return O.attention_sparse(*args, out=out, rows=rows, nthreads=threads)
+        return run, work, f"{len(rows)} of {self.S} query rows, all heads; rate extrapolated linearly in rows"
+
+    def check(self, O):
+        import numpy as np
+        rows = np.linspace(0, self.S - 1, 24).astype(np.uint32)
+        out = np.zeros((self.S, self.H * self.D), np.float32)
+        O.attention_sparse(*self._args(O), out=out, rows=rows)
+        return self.o.cpu().numpy()[rows], out[rows], f"{len(rows)} query rows x all heads"
+
+
+def torch_int16():
+    import torch
+    return torch.int16
+
+
+def make_workload(name):
+    if name == "decode":
+        return Decode()
+    if name == "prefill":
+        return Prefill("prefill", "prefill attention TFLOP/s (causal GQA)", 2, 32, 8, 128, 8192, "bf16", 0.5,
+                       UINT32_MAX, 0, cfg="prefill (configs[2])")
+    if name == "prefill_small":
+        return Prefill("prefill_small", "prefill attention TFLOP/s (causal GQA)", 1, 16, 8, 128, 512, "fp16", 1.0,
+                       UINT32_MAX, 0, cfg="prefill_small (configs[0])")
+    if name == "bidir":
+        return Prefill("bidir", "bidirectional attention TFLOP/s (video DiT)", 1, 24, 24, 128, 75600, "bf16", 1.0, 0,
+                       0, rms_qk=True, cfg="bidir (configs[4])")
+    if name == "sparse":
+        return Sparse()
+    raise SystemExit(f"unknown workload {name}")
+
+
+# ---- clocks ---------------------------------------------------------------------------------------------------------
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- runs -----------------------------------------------------------------------------------------------------------
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    import torch
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=DEVICE)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def read_traffic(name):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary (None if not captured)."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == name and not line.startswith("#"):
+                return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+def run_mako(args):
+    import torch
+    import mako_attn
+    import oracle as O
+    import attn_cases as C
+
+    world, rank, local = dist_setup()
+    W = make_workload(args.workload)
+    ctx = mako_attn.Context(local)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE)
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        W.step(ctx)
+    barrier(world)
+    launches0 = ctx.launches()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    times = []
+    barrier(world)
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        W.step(ctx)
+        e1.record(stream)
+        times.append((e0, e1))
+    barrier(world)
+    clk = clocks.stop()
+    launches = ctx.launches() - launches0
+    ms = [a.elapsed_time(b) for a, b in times]
+    total_ms = max_over_ranks(sum(ms), world)
+    ms_step = total_ms / args.steps
+    work = W.work()
+    value = W.to_metric(work * world / (ms_step / 1e3))
+
+    # end to end through the public API: pinned host inputs in, output back, every step
+    host_in = [t.cpu().pin_memory() for t in W.inputs]
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in W.outputs]
+    dev_in = W.inputs
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    e2e_times = []
+    barrier(world)
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        W.step(ctx)
+        for h, d in zip(host_out, W.outputs):
+            h.copy_(d, non_blocking=True)
+        e1.record(stream)
+        if i >= args.warmup:
+            e2e_times.append((e0, e1))
+    barrier(world)
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_times), world) / args.steps
+    e2e_value = W.to_metric(work * world / (e2e_ms / 1e3))
+
+    hbm, tflops, src = peaks()
+    per_launch_ms = statistics.mean(ms)
+    if W.bound == "hbm":
+        achieved = work / (per_launch_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "peak_source": src}
+    else:
+        achieved = work / (per_launch_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
+                "frac": round(achieved / tflops, 4), "peak_source": src}
+    roof["traffic"] = read_traffic(W.name)
+    roof["timed"] = "whole C-ABI call per step (all its kernels), CUDA events on the launching stream"
+
+    # parity of this run's output against the oracle on a sample, and the CPU baseline (rank 0, N = 1)
+    parity = cpu = None
+    if rank == 0:
+        got, want, what = W.check(O)
+        a, r, w = C.compare(got, want)
+        parity = {"max_abs": float(f"{a:.3e}"), "rel_l2": float(f"{r:.3e}"), "rows": what,
+                  "within_tolerance": bool(a <= C.MAX_ABS and r <= C.REL_L2)}
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(W, O)
+
+    if rank == 0:
+        line = {
+            "metric": W.metric, "value": round(value, 3), "unit": W.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded normal)",
+            "config": dict(W.config, parallelism=f"replica x{world}" if world > 1 else "single GPU"),
+            "e2e": {"value": round(e2e_value, 3), "unit": W.unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": launches, "roofline": roof, "clocks": clk, "parity": parity, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def cpu_baseline(W, O, min_seconds=5.0):
+    """The oracle on this host's cores over W's sample, repeated for at least min_seconds."""
+    threads = O.threads(0)
+    run, work, sample = W.cpu_sample(O, threads)
+    run()  # warm (page-in, thread pool)
+    t0 = time.perf_counter()
+    steps = 0
+    while True:
+        run()
+        steps += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": round(W.to_metric(work / dt), 6), "unit": W.unit, "cores": threads, "kind": "port",
+            "sample": sample, "seconds": round(dt, 3)}
+
+
+def run_reference(args):
+    """The reference arm: the oracle's restatement of the reference's scalar attention on all host threads."""
+    global DEVICE
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle as O
+    DEVICE = "cpu"
+    W = make_workload(args.workload)
+    threads = O.threads(0)
+    run, work, sample = W.cpu_sample(O, threads)
+    for _ in range(args.warmup):
+        run()
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        ts.append(time.perf_counter() - t0)
+    dt = statistics.mean(ts)
+    value = W.to_metric(work / dt)
+    line = {"impl": "reference", "metric": W.metric, "value": round(value, 6), "unit": W.unit,
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": W.dtype, "data": "synthetic (seeded normal)", "config": W.config,
+            "cpu_baseline": {"value": round(value, 6), "unit": W.unit, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 6), "unit": W.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "mako-common's attention is Metal-only (Apple GPUs); its scalar C++ reference attention "
+                    "(tests/sparse_attn_test.cpp:131-180) restated in oracle/ runs here with OpenMP"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "sparse", "bidir", "prefill_small"])
+    ap.add_argument("--impl", default="mako", choices=["mako", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mako(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,120 @@
+/* mako_attn.h -- C ABI of the B200 (sm_100a) attention path for mako-common.
+ *
+ * This library replaces the attention slice of mako-common's Metal dispatch glue (src/gpu/runtime.{hpp,cpp},
+ * src/mtl/) and kernels (src/kernels/ops.metal attention kernels).  Each entry point below names the reference
+ * interface it replaces.  Conventions for every call:
+ *   - pointers are CUDA device pointers (16-byte aligned) unless a comment says host;
+ *   - `stream` is a cudaStream_t (NULL: the legacy default stream); calls only enqueue work, never synchronise;
+ *   - tensors are owned by the caller; the context owns its scratch (like gpu::Runtime::scratch,
+ *     src/gpu/runtime.cpp:117-125), so one context serves one thread / one stream at a time;
+ *   - the return value is MAKO_OK or a negative code; mako_attn_last_error() gives this thread's message for the
+ *     last failure.  Argument errors are reported before anything is enqueued (the reference throws
+ *     std::runtime_error at the same points: src/models/runtime.cpp:266-267,290-291,311-312).
+ * Element types: MAKO_F16 (IEEE half, the reference's `half` tiles) or MAKO_BF16.  Outputs are fp32 as in the
+ * reference (o [n_q][width] floats, head h at column h * dim).
+ */
+#ifndef MAKO_ATTN_H
+#define MAKO_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MAKO_ATTN_VERSION 1
+
+enum { MAKO_F16 = 0, MAKO_BF16 = 1 };
+
+enum {
+    MAKO_OK = 0,
+    MAKO_EINVAL = -22,  /* an argument the call cannot take */
+    MAKO_ENOMEM = -12,  /* scratch allocation failed */
+    MAKO_ECUDA = -5,    /* a CUDA call failed (launch error, bad device) */
+    MAKO_ENOTSUP = -95  /* a combination this build does not provide */
+};
+
+/* Options for mako_attn_set_option. */
+enum {
+    /* Dense attention kernel for 128-wide heads: 0 automatic (tcgen05 where built), 1 the portable mma.sync kernel,
+     * 2 the tcgen05 kernel (MAKO_ENOTSUP where it cannot run). */
+    MAKO_OPT_PREFILL_KERNEL = 1,
+    /* 1 (default): mako_attention with n_q == 1 runs the split-KV decode kernel; 0: the prefill kernel. */
+    MAKO_OPT_DECODE_ROUTE = 2
+};
+
+typedef struct mako_attn_ctx mako_attn_ctx;
+
+/* This thread's message for its last failed call ("" if none). */
+const char* mako_attn_last_error(void);
+int mako_attn_version(void);
+
+/* A context on CUDA device `device`: its scratch buffers and options.  Replaces gpu::Runtime's scratch and
+ * pipeline cache (src/gpu/runtime.cpp:117-135); destroy frees the scratch (synchronising the device). */
+int mako_attn_create(int device, mako_attn_ctx** out);
+int mako_attn_destroy(mako_attn_ctx* ctx);
+int mako_attn_set_option(mako_attn_ctx* ctx, int option, int64_t value);
+/* Kernel launches this context has enqueued since it was created (a counter for profiling harnesses; the
+ * reference's equivalent is its per-kernel telemetry, src/gpu/runtime.cpp:343-370). */
+int mako_attn_launches(mako_attn_ctx* ctx, uint64_t* out);
+
+/* Flash attention over 16-bit head tiles: q [heads][q_pad][dim], k and v [kv_heads][k_pad][dim] into
+ * o [n_q][width] floats, head h at column h * dim and reading kv head h / (heads / kv_heads).  Key j is visible to
+ * query i (position pos = q_pos0 + i) when j < n_k and (j <= pos or (pos >= block and j >= block)):
+ * block = 0 bidirectional, block = UINT32_MAX causal.  dim 64, 128 or 256; width 0 means heads * dim.  Rows that
+ * see no key are 0.  Padded key / value rows [n_k, k_pad) must hold finite values (the reference zeroes them).
+ * Replaces TransformerRuntime::attention (src/models/runtime.hpp:90-95, src/models/runtime.cpp:262-273); the
+ * reference computes width as heads * dim.  q_pad must be a multiple of 64 and at least n_q (the reference's grid,
+ * q_pad / 64 tiles of 64 rows), k_pad at least n_k.  n_q == 1 runs the split-KV decode kernel. */
+int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v, float* o,
+                   uint32_t n_q, uint32_t q_pad, uint32_t n_k, uint32_t k_pad, uint32_t heads, uint32_t kv_heads,
+                   uint32_t q_pos0, uint32_t block, uint32_t dim, uint32_t width);
+
+/* Batched single-token decode over a KV cache of varying lengths: q [batch][heads][dim],
+ * k and v [batch][kv_heads][k_stride][dim], kv_len [batch] int32 on the device (each at most max_kv_len and at most
+ * k_stride), o [batch][heads * dim] floats.  Sequence b's query attends keys [0, kv_len[b]); a length <= 0 gives 0.
+ * No reference counterpart kernel: the reference's decode step is mako_attention's form with n_q = 1,
+ * q_pos0 = len - 1, block = UINT32_MAX (src/models/runtime.cpp:262-273), looped over sequences by the caller. */
+int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v,
+                          float* o, uint32_t batch, const int32_t* kv_len, uint32_t max_kv_len, uint32_t heads,
+                          uint32_t kv_heads, uint32_t dim, uint32_t k_stride);
+
+/* Cube selection for block-sparse attention over 128-wide heads: per head and query cube (64 rows), the `topk`
+ * key cubes whose mean-pooled k scores highest against the cube's mean-pooled q (cnt[c]: valid rows of cube c,
+ * device uint32 [n_cubes]; invalid rows must be zero).  local 0: by score; 1: the query cube itself first; 3: also
+ * the cubes `stride` before and after.  *sel receives [heads][n_cubes][min(topk, n_cubes)] uint16 and *nsel
+ * [heads][n_cubes] uint16, both device scratch owned by ctx and valid until its next mako_cube_select.
+ * Replaces TransformerRuntime::cube_select (src/models/runtime.hpp:96-108, src/models/runtime.cpp:286-303):
+ * n_cubes <= 4096, topk > 0, local in {0, 1, 3}; also n_cubes * 64 <= q_pad and <= k_pad. */
+int mako_cube_select(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, uint32_t heads,
+                     uint32_t q_pad, uint32_t k_pad, uint32_t n_cubes, const uint32_t* cnt, uint32_t topk,
+                     uint16_t** sel, uint16_t** nsel, uint32_t local, uint32_t stride);
+
+/* Block-sparse attention over 128-wide heads: query tile t < n_cubes (rows 64 t .. 64 t + 63) attends the valid
+ * rows of its selected cubes (sel [heads][n_cubes][min(topk, n_cubes)], nsel [heads][n_cubes], as
+ * mako_cube_select returns them; an entry listed twice counts twice, entries >= n_cubes are skipped) and the valid
+ * rows of [dense0, dense1); a later tile attends every valid key below n_k.  valid [k_pad] uint8; query row r's
+ * output goes to o row map[r] (map [q_pad] int32, < 0: dropped).  Replaces TransformerRuntime::attention_sparse
+ * (src/models/runtime.hpp:109-111, src/models/runtime.cpp:305-317): q_pad a multiple of 64, k_pad of 128, dense0
+ * of 32; also dense0 <= dense1 <= k_pad, n_cubes * 64 <= q_pad and <= k_pad, width >= heads * 128. */
+int mako_attention_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v,
+                          float* o, uint32_t n_q, uint32_t q_pad, uint32_t n_k, uint32_t k_pad, uint32_t heads,
+                          uint32_t kv_heads, uint32_t width, uint32_t n_cubes, uint32_t topk, uint32_t dense0,
+                          uint32_t dense1, const uint16_t* sel, const uint16_t* nsel, const uint8_t* valid,
+                          const int32_t* map);
+
+/* Block-sparse attention from kept-block lists: n rows (a multiple of 64) of 64-row blocks, query block t of head
+ * h attends the key blocks lists[h][t][0 .. counts[h][t]) (int32 device arrays, [heads][n / 64][max_list] and
+ * [heads][n / 64]); every key valid, output row r to o row r (width heads * 128).  The same kernel as
+ * mako_attention_sparse with no dense rows, an all-valid mask and the identity map -- the form H3's cube layout
+ * takes when every row is a full cube (src/models/h3.cpp:510-546). */
+int mako_attention_block_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k,
+                                const void* v, float* o, uint32_t n, uint32_t heads, uint32_t kv_heads,
+                                const int32_t* lists, const int32_t* counts, uint32_t max_list);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MAKO_ATTN_H */

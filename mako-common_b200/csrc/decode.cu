@@ -1,0 +1,274 @@
+// Split-KV decode: one query row per (sequence, head) attending keys [0, len) of its sequence's cache.  The reference
+// has no decode kernel (a decode token there is attention() with n_q = 1, q_pos0 = len - 1, causal:
+// src/models/runtime.cpp:262-273, src/kernels/ops.metal:242-270); this is the same maths laid out for an HBM-bound
+// read of the whole cache.
+//
+// Kernel 1 (decode_split_kernel): one CTA per (split of `chunk` keys, kv head, sequence) serves the q heads of that
+// kv head's GQA group (up to 16 a CTA) from one read of K and V.  64-key tiles of K and V stream through a 3-stage
+// cp.async ring of 128-bit loads into XOR-swizzled shared memory; each of the 4 warps takes 16 keys of a tile on
+// mma.sync (the group's q rows padded to 16), keeps its own running softmax and accumulator, and the warps merge at
+// the end into one partial (o unnormalised, max, sum) per (sequence, head, split).
+// Kernel 2 (decode_combine_kernel): the log-sum-exp merge of a row's splits into o.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <type_traits>
+
+namespace mako {
+namespace {
+
+constexpr int DBN = 64, DNT = 128, DST = 3, QR = 16;
+
+template <int D, typename T>
+__global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams p)
+{
+    constexpr int ROWB = D * 2, CH = D / 8, KS = D / 16, TILE = DBN * ROWB;
+    constexpr bool SPLIT = !std::is_same<T, __half>::value;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t sQ = smem_u32(smem), sK = sQ + QR * ROWB, sV = sK + DST * TILE;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3, mi = lane >> 3;
+    const uint32_t group = p.heads / p.kv_heads, rb = (group + QR - 1) / QR;
+    const uint32_t b = blockIdx.z, kvh = blockIdx.y / rb, rblk = blockIdx.y % rb, split = blockIdx.x;
+    const int32_t lraw = p.kv_len ? p.kv_len[b] : int32_t(p.len);
+    const uint32_t L = lraw > 0 ? uint32_t(lraw) : 0u;
+    const uint32_t start = split * p.chunk;
+    if (start >= L)
+        return;
+    const uint32_t end = min(L, start + p.chunk);
+    const uint32_t h0 = kvh * group + rblk * QR, nrows = min(uint32_t(QR), group - rblk * QR);
+    const T* qg = static_cast<const T*>(p.q) + uint64_t(b) * p.q_bstride;
+    const T* kg = static_cast<const T*>(p.k) + uint64_t(b) * p.k_bstride + uint64_t(kvh) * p.k_hstride;
+    const T* vg = static_cast<const T*>(p.v) + uint64_t(b) * p.k_bstride + uint64_t(kvh) * p.k_hstride;
+
+    for (int i = tid; i < QR * CH; i += DNT) {
+        const uint32_t r = i / CH, c = i % CH;
+        const bool ok = r < nrows;
+        cp_async16(sQ + swz(r, c, ROWB), qg + (ok ? uint64_t(h0 + r) * p.q_hstride + c * 8 : 0), ok);
+    }
+    cp_async_commit();
+    const uint32_t nt = (end - start + DBN - 1) / DBN;
+    auto load = [&](uint32_t t) {
+        const uint32_t st = t % DST, j0 = start + t * DBN;
+        for (int i = tid; i < DBN * CH; i += DNT) {
+            const uint32_t r = i / CH, c = i % CH, j = j0 + r;
+            const bool ok = j < end;
+            const uint64_t off = ok ? uint64_t(j) * D + c * 8 : 0;
+            cp_async16(sK + st * TILE + swz(r, c, ROWB), kg + off, ok);
+            cp_async16(sV + st * TILE + swz(r, c, ROWB), vg + off, ok);
+        }
+    };
+#pragma unroll
+    for (int t = 0; t < DST - 1; ++t) {
+        if (uint32_t(t) < nt)
+            load(t);
+        cp_async_commit();
+    }
+
+    uint32_t qa[KS][4];
+    float acc[D / 8][4];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i)
+        acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+    const float scale = p.scale * kLog2e;
+
+    for (uint32_t t = 0; t < nt; ++t) {
+        cp_async_wait<DST - 2>();
+        __syncthreads();
+        if (t == 0) {
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks)
+                ldsm_x4(qa[ks], sQ + swz((mi & 1) * 8 + (lane & 7), ks * 2 + (mi >> 1), ROWB));
+        }
+        if (t + DST - 1 < nt)
+            load(t + DST - 1);
+        cp_async_commit();
+        const uint32_t kst = sK + (t % DST) * TILE, vst = sV + (t % DST) * TILE;
+        const uint32_t kr = warp * 16;  // this warp's 16 keys of the tile
+
+        float s[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            uint32_t kb[4];
+            ldsm_x4(kb, kst + swz(kr + (mi >> 1) * 8 + (lane & 7), ks * 2 + (mi & 1), ROWB));
+            mma16816(s[0], qa[ks], kb[0], kb[1], T());
+            mma16816(s[1], qa[ks], kb[2], kb[3], T());
+        }
+        const uint32_t jb = start + t * DBN + kr;
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t j = jb + n * 8 + 2 * tq + (e & 1);
+                const float x = j < end ? s[n][e] * scale : -INFINITY;
+                s[n][e] = x;
+                mx[e >> 1] = fmaxf(mx[e >> 1], x);
+            }
+        float f[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            const float mn = fmaxf(m[r], mx[r]);
+            f[r] = mn == -INFINITY ? 1.0f : ex2(m[r] - mn);
+            m[r] = mn;
+            l[r] *= f[r];
+        }
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) {
+            acc[i][0] *= f[0];
+            acc[i][1] *= f[0];
+            acc[i][2] *= f[1];
+            acc[i][3] *= f[1];
+        }
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float mm = m[e >> 1];
+                const float pe = mm == -INFINITY ? 0.0f : ex2(s[n][e] - mm);
+                s[n][e] = pe;
+                l[e >> 1] += pe;
+            }
+        uint32_t pa[4], pl[4];
+        if (!SPLIT) {
+            pa[0] = Elem<__half>::pack(s[0][0], s[0][1]);
+            pa[1] = Elem<__half>::pack(s[0][2], s[0][3]);
+            pa[2] = Elem<__half>::pack(s[1][0], s[1][1]);
+            pa[3] = Elem<__half>::pack(s[1][2], s[1][3]);
+        } else {
+            const float* src[4] = {&s[0][0], &s[0][2], &s[1][0], &s[1][2]};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const __nv_bfloat16 h0 = __float2bfloat16_rn(src[i][0]), h1 = __float2bfloat16_rn(src[i][1]);
+                pa[i] = Elem<__nv_bfloat16>::pack(__bfloat162float(h0), __bfloat162float(h1));
+                pl[i] = Elem<__nv_bfloat16>::pack(src[i][0] - __bfloat162float(h0), src[i][1] - __bfloat162float(h1));
+            }
+        }
+#pragma unroll
+        for (int dp = 0; dp < D / 16; ++dp) {
+            uint32_t vb[4];
+            ldsm_x4_t(vb, vst + swz(kr + (mi & 1) * 8 + (lane & 7), dp * 2 + (mi >> 1), ROWB));
+            mma16816(acc[2 * dp], pa, vb[0], vb[1], T());
+            mma16816(acc[2 * dp + 1], pa, vb[2], vb[3], T());
+            if (SPLIT) {
+                mma16816(acc[2 * dp], pl, vb[0], vb[1], T());
+                mma16816(acc[2 * dp + 1], pl, vb[2], vb[3], T());
+            }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // the stage ring is reused below for the warps' merge
+
+    // Merge the four warps: rows g and g + 8 of each warp's state into shared memory, then per row.
+    float* sm = reinterpret_cast<float*>(smem + QR * ROWB);  // [4][2][QR] (m, l) then [4][QR][D] o
+    float* so = sm + 4 * 2 * QR;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
+        if (tq == 0) {
+            sm[(warp * 2 + 0) * QR + g + 8 * r] = m[r];
+            sm[(warp * 2 + 1) * QR + g + 8 * r] = l[r];
+        }
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i)
+            *reinterpret_cast<float2*>(so + (warp * QR + g + 8 * r) * D + i * 8 + 2 * tq) =
+                make_float2(acc[i][2 * r], acc[i][2 * r + 1]);
+    }
+    __syncthreads();
+    for (uint32_t i = tid; i < nrows * D; i += DNT) {
+        const uint32_t r = i / D, d = i % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w)
+            M = fmaxf(M, sm[(w * 2) * QR + r]);
+        float Ls = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float mw = sm[(w * 2) * QR + r];
+            const float fw = mw == -INFINITY ? 0.0f : ex2(mw - M);
+            Ls += sm[(w * 2 + 1) * QR + r] * fw;
+            O += so[(w * QR + r) * D + d] * fw;
+        }
+        const uint64_t row = (uint64_t(b) * p.heads + h0 + r) * p.n_splits + split;
+        p.o_part[row * D + d] = O;
+        if (d == 0)
+            p.ml_part[row] = make_float2(M, Ls);
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p)
+{
+    const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int32_t lraw = p.kv_len ? p.kv_len[b] : int32_t(p.len);
+    const uint32_t L = lraw > 0 ? uint32_t(lraw) : 0u;
+    const uint32_t ns = min((L + p.chunk - 1) / p.chunk, p.n_splits);
+    const uint64_t row0 = (uint64_t(b) * p.heads + h) * p.n_splits;
+    float M = -INFINITY;
+    for (uint32_t s = 0; s < ns; ++s)
+        M = fmaxf(M, p.ml_part[row0 + s].x);
+    float Ls = 0.0f, O = 0.0f;
+    for (uint32_t s = 0; s < ns; ++s) {
+        const float2 ml = p.ml_part[row0 + s];
+        const float f = ml.x == -INFINITY ? 0.0f : ex2(ml.x - M);
+        Ls += ml.y * f;
+        O += p.o_part[(row0 + s) * D + d] * f;
+    }
+    p.o[uint64_t(b) * p.o_bstride + uint64_t(h) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
+}
+
+template <int D, typename T>
+cudaError_t launch_dec(const DecodeParams& p, cudaStream_t st)
+{
+    constexpr int smem = (QR + 2 * DST * DBN) * D * 2;
+    static_assert((4 * 2 * QR + 4 * QR * D) * 4 <= 2 * DST * DBN * D * 2, "merge buffer fits the stage ring");
+    auto kern = decode_split_kernel<D, T>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess)
+        return e;
+    const uint32_t group = p.heads / p.kv_heads, rb = (group + QR - 1) / QR;
+    kern<<<dim3(p.n_splits, p.kv_heads * rb, p.batch), DNT, smem, st>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return e;
+    decode_combine_kernel<D><<<dim3(p.heads, p.batch), D, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+} // namespace
+
+void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t heads, int num_sms, uint32_t* chunk,
+                 uint32_t* n_splits)
+{
+    // Small chunks keep the tail short (the hardware scheduler back-fills freed SMs); at least ~8 CTAs an SM.
+    const uint32_t group = heads / kv_heads, rb = (group + QR - 1) / QR;
+    const uint64_t rows = uint64_t(max_len) * batch * kv_heads * rb;
+    const uint64_t target = uint64_t(num_sms > 0 ? num_sms : 148) * 8;
+    uint64_t c = (rows + target - 1) / target;
+    c = (c + DBN - 1) / DBN * DBN;
+    c = c < 256 ? 256 : (c > 1024 ? 1024 : c);
+    *chunk = uint32_t(c);
+    *n_splits = max_len ? uint32_t((max_len + c - 1) / c) : 1u;
+}
+
+cudaError_t launch_decode(const DecodeParams& p, int dtype, int dim, cudaStream_t st)
+{
+    if (p.batch == 0 || p.heads == 0)
+        return cudaSuccess;
+    const bool bf = dtype == kBF16;
+    switch (dim) {
+    case 64:
+        return bf ? launch_dec<64, __nv_bfloat16>(p, st) : launch_dec<64, __half>(p, st);
+    case 128:
+        return bf ? launch_dec<128, __nv_bfloat16>(p, st) : launch_dec<128, __half>(p, st);
+    case 256:
+        return bf ? launch_dec<256, __nv_bfloat16>(p, st) : launch_dec<256, __half>(p, st);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
+
+} // namespace mako

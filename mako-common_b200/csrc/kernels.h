@@ -1,0 +1,64 @@
+// Internal launch interface between the C ABI (mako_attn.cu) and the kernels.  Plain structs, device pointers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mako {
+
+enum Dtype : int { kF16 = 0, kBF16 = 1 };
+
+// One attention launch: the fields of the reference's AttnArgs (src/kernels/ops.metal:54-64) plus, for the
+// block-sparse form, those of SparseAttnArgs (ops.metal:1029-1034) and its index buffers.
+struct AttnParams {
+    const void* q;  // [heads][q_pad][dim]
+    const void* k;  // [kv_heads][k_pad][dim]
+    const void* v;  // [kv_heads][k_pad][dim]
+    float* o;       // [rows][width], head h at column h * dim
+    uint32_t n_q, q_pad, n_k, k_pad, heads, kv_heads, q_pos0, block, width;
+    float scale;  // softmax scale (1 / sqrt(dim))
+    // block-sparse pass list
+    uint32_t n_cubes, max_sel, dense0, dense1;
+    const void* sel;       // [heads][n_cubes][max_sel] uint16 (cube_select) or int32 (kept-block lists)
+    const void* nsel;      // [heads][n_cubes], same integer type as sel
+    const uint8_t* valid;  // [k_pad] key validity, null: every key valid
+    const int32_t* map;    // [q_pad] output row per query row (< 0 dropped), null: identity
+};
+
+// Portable flash attention on mma.sync tensor cores, any head width of 64 / 128 / 256.
+cudaError_t launch_attn_mma(const AttnParams& p, int dtype, int dim, bool sparse, bool sel_i32, cudaStream_t s);
+
+// Split-KV decode: one query row per (sequence, head) over keys [0, len).
+struct DecodeParams {
+    const void* q;  // query row of (b, h) at q + b * q_bstride + h * q_hstride
+    const void* k;  // key row j of (b, kvh) at k + b * k_bstride + kvh * k_hstride + j * dim
+    const void* v;  // as k
+    float* o;       // output of (b, h) at o + b * o_bstride + h * dim
+    float* o_part;  // scratch [batch][heads][n_splits][dim]
+    float2* ml_part;  // scratch [batch][heads][n_splits]: (max in log2 units, sum)
+    const int32_t* kv_len;  // device [batch] lengths, or null: `len` for every sequence
+    uint32_t len;
+    uint64_t q_bstride, q_hstride, k_bstride, k_hstride, o_bstride;  // in elements
+    uint32_t batch, heads, kv_heads, chunk, n_splits;
+    float scale;
+};
+// Keys a split takes and how many splits, for the longest sequence max_len.
+void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t heads, int num_sms, uint32_t* chunk,
+                 uint32_t* n_splits);
+cudaError_t launch_decode(const DecodeParams& p, int dtype, int dim, cudaStream_t s);
+
+// cube_select: pooled means, their scores, the top k per (head, query cube).
+struct CubeParams {
+    const void* q;
+    const void* k;
+    const uint32_t* cnt;
+    float* qp;  // scratch [heads][n_cubes][128]
+    float* kp;  // scratch [heads][n_cubes][128]
+    float* sc;  // scratch [heads][n_cubes][n_cubes]
+    uint16_t* sel;   // [heads][n_cubes][min(topk, n_cubes)]
+    uint16_t* nsel;  // [heads][n_cubes]
+    uint32_t heads, q_pad, k_pad, n_cubes, topk, local, stride;
+};
+cudaError_t launch_cube_select(const CubeParams& p, int dtype, cudaStream_t s);
+
+} // namespace mako

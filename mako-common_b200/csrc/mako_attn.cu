@@ -1,0 +1,454 @@
+// The C ABI (include/mako_attn.h): argument checks, the context's scratch, kernel choice, launch.  Replaces the
+// attention slice of mako-common's gpu::Runtime (scratch by name src/gpu/runtime.cpp:117-125, dispatch :243-259,
+// error check in finish :453-475) and of TransformerRuntime (src/models/runtime.cpp:262-317).
+#include "kernels.h"
+#include "mako_attn.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <unordered_map>
+
+struct mako_attn_ctx {
+    int device = 0;
+    int num_sms = 148;
+    int prefill_kernel = 0;  // MAKO_OPT_PREFILL_KERNEL
+    int decode_route = 1;    // MAKO_OPT_DECODE_ROUTE
+    uint64_t launches = 0;   // kernels enqueued
+    struct Buf {
+        void* ptr = nullptr;
+        size_t bytes = 0;
+    };
+    std::unordered_map<std::string, Buf> scratch;
+};
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_error = buf;
+    return code;
+}
+
+int cuda_fail(const char* what, cudaError_t e)
+{
+    return fail(MAKO_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Runs the calls of one entry point with the context's device current, the caller's device restored after.
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceGuard(int dev)
+    {
+        if ((err = cudaGetDevice(&prev)) == cudaSuccess && prev != dev)
+            err = cudaSetDevice(dev);
+    }
+    ~DeviceGuard()
+    {
+        int cur;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev)
+            cudaSetDevice(prev);
+    }
+};
+
+// A named scratch buffer of at least `bytes`, grown (never shrunk) on demand like gpu::Runtime::scratch.
+int scratch(mako_attn_ctx* ctx, const char* name, size_t bytes, void** out)
+{
+    auto& b = ctx->scratch[name];
+    if (b.bytes < bytes) {
+        if (b.ptr) {
+            cudaError_t e = cudaFree(b.ptr);  // synchronises with work still reading it
+            b.ptr = nullptr;
+            b.bytes = 0;
+            if (e != cudaSuccess)
+                return cuda_fail("scratch free", e);
+        }
+        cudaError_t e = cudaMalloc(&b.ptr, bytes);
+        if (e != cudaSuccess) {
+            b.ptr = nullptr;
+            cudaGetLastError();
+            return fail(MAKO_ENOMEM, "scratch %s: %zu bytes: %s", name, bytes, cudaGetErrorString(e));
+        }
+        b.bytes = bytes;
+    }
+    *out = b.ptr;
+    return MAKO_OK;
+}
+
+int check_ctx(mako_attn_ctx* ctx, int dtype)
+{
+    if (!ctx)
+        return fail(MAKO_EINVAL, "null context");
+    if (dtype != MAKO_F16 && dtype != MAKO_BF16)
+        return fail(MAKO_EINVAL, "element type %d (MAKO_F16 or MAKO_BF16)", dtype);
+    return MAKO_OK;
+}
+
+int launched(const char* what, cudaError_t e)
+{
+    if (e != cudaSuccess)
+        return cuda_fail(what, e);
+    g_error.clear();
+    return MAKO_OK;
+}
+
+} // namespace
+
+extern "C" {
+
+const char* mako_attn_last_error(void) { return g_error.c_str(); }
+
+int mako_attn_version(void) { return MAKO_ATTN_VERSION; }
+
+int mako_attn_create(int device, mako_attn_ctx** out)
+{
+    if (!out)
+        return fail(MAKO_EINVAL, "null output pointer");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess)
+        return cuda_fail("cudaGetDeviceCount", e);
+    if (device < 0 || device >= n)
+        return fail(MAKO_EINVAL, "device %d of %d", device, n);
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess)
+        return cuda_fail("cudaGetDeviceProperties", e);
+    auto* ctx = new (std::nothrow) mako_attn_ctx;
+    if (!ctx)
+        return fail(MAKO_ENOMEM, "context");
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    *out = ctx;
+    g_error.clear();
+    return MAKO_OK;
+}
+
+int mako_attn_destroy(mako_attn_ctx* ctx)
+{
+    if (!ctx)
+        return MAKO_OK;
+    int rc = MAKO_OK;
+    {
+        DeviceGuard dg(ctx->device);
+        for (auto& kv : ctx->scratch)
+            if (kv.second.ptr) {
+                cudaError_t e = cudaFree(kv.second.ptr);
+                if (e != cudaSuccess && rc == MAKO_OK)
+                    rc = cuda_fail("scratch free", e);
+            }
+    }
+    delete ctx;
+    return rc;
+}
+
+int mako_attn_set_option(mako_attn_ctx* ctx, int option, int64_t value)
+{
+    if (!ctx)
+        return fail(MAKO_EINVAL, "null context");
+    switch (option) {
+    case MAKO_OPT_PREFILL_KERNEL:
+        if (value < 0 || value > 2)
+            return fail(MAKO_EINVAL, "prefill kernel %lld (0 auto, 1 mma.sync, 2 tcgen05)", (long long)value);
+        ctx->prefill_kernel = int(value);
+        return MAKO_OK;
+    case MAKO_OPT_DECODE_ROUTE:
+        ctx->decode_route = value != 0;
+        return MAKO_OK;
+    default:
+        return fail(MAKO_EINVAL, "option %d", option);
+    }
+}
+
+int mako_attn_launches(mako_attn_ctx* ctx, uint64_t* out)
+{
+    if (!ctx || !out)
+        return fail(MAKO_EINVAL, "null argument");
+    *out = ctx->launches;
+    return MAKO_OK;
+}
+
+int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v, float* o,
+                   uint32_t n_q, uint32_t q_pad, uint32_t n_k, uint32_t k_pad, uint32_t heads, uint32_t kv_heads,
+                   uint32_t q_pos0, uint32_t block, uint32_t dim, uint32_t width)
+{
+    if (int rc = check_ctx(ctx, dtype))
+        return rc;
+    if (dim != 64 && dim != 128 && dim != 256)
+        return fail(MAKO_EINVAL, "attention: heads of %u", dim);
+    if (width == 0)
+        width = heads * dim;
+    if (!heads || !kv_heads || heads % kv_heads)
+        return fail(MAKO_EINVAL, "attention: %u heads over %u kv heads", heads, kv_heads);
+    if (q_pad % 64 || q_pad < n_q || k_pad < n_k)
+        return fail(MAKO_EINVAL, "attention: q_pad %u (a multiple of 64, at least n_q %u), k_pad %u (at least n_k %u)",
+                    q_pad, n_q, k_pad, n_k);
+    if (width < heads * dim)
+        return fail(MAKO_EINVAL, "attention: o rows of %u floats for %u heads of %u", width, heads, dim);
+    if (!q || !k || !v || !o || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(MAKO_EINVAL, "attention: null or unaligned tensor (16-byte alignment)");
+    if (n_q == 0)
+        return MAKO_OK;
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    auto st = static_cast<cudaStream_t>(stream);
+    if (n_q == 1 && ctx->decode_route) {
+        // One query: the keys it sees are a prefix [0, len) (mask predicate at pos = q_pos0).
+        const uint32_t len = q_pos0 >= block ? n_k : (n_k < q_pos0 + 1 ? n_k : q_pos0 + 1);
+        mako::DecodeParams p{};
+        p.q = q;
+        p.k = k;
+        p.v = v;
+        p.o = o;
+        p.kv_len = nullptr;
+        p.len = len;
+        p.q_bstride = 0;
+        p.q_hstride = uint64_t(q_pad) * dim;
+        p.k_bstride = 0;
+        p.k_hstride = uint64_t(k_pad) * dim;
+        p.o_bstride = width;
+        p.batch = 1;
+        p.heads = heads;
+        p.kv_heads = kv_heads;
+        p.scale = 1.0f / sqrtf(float(dim));
+        mako::decode_plan(len, 1, kv_heads, heads, ctx->num_sms, &p.chunk, &p.n_splits);
+        void *op, *mlp;
+        if (int rc = scratch(ctx, "dec_o", size_t(heads) * p.n_splits * dim * 4, &op))
+            return rc;
+        if (int rc = scratch(ctx, "dec_ml", size_t(heads) * p.n_splits * 8, &mlp))
+            return rc;
+        p.o_part = static_cast<float*>(op);
+        p.ml_part = static_cast<float2*>(mlp);
+        ctx->launches += 2;
+        return launched("attention (decode)", mako::launch_decode(p, dtype, dim, st));
+    }
+    mako::AttnParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = o;
+    p.n_q = n_q;
+    p.q_pad = q_pad;
+    p.n_k = n_k;
+    p.k_pad = k_pad;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.q_pos0 = q_pos0;
+    p.block = block;
+    p.width = width;
+    p.scale = 1.0f / sqrtf(float(dim));
+    if (ctx->prefill_kernel == 2)
+        return fail(MAKO_ENOTSUP, "attention: the tcgen05 kernel is not in this build");
+    ctx->launches += 1;
+    return launched("attention", mako::launch_attn_mma(p, dtype, dim, false, false, st));
+}
+
+int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v,
+                          float* o, uint32_t batch, const int32_t* kv_len, uint32_t max_kv_len, uint32_t heads,
+                          uint32_t kv_heads, uint32_t dim, uint32_t k_stride)
+{
+    if (int rc = check_ctx(ctx, dtype))
+        return rc;
+    if (dim != 64 && dim != 128 && dim != 256)
+        return fail(MAKO_EINVAL, "decode: heads of %u", dim);
+    if (!heads || !kv_heads || heads % kv_heads)
+        return fail(MAKO_EINVAL, "decode: %u heads over %u kv heads", heads, kv_heads);
+    if (max_kv_len > k_stride)
+        return fail(MAKO_EINVAL, "decode: max_kv_len %u beyond the cache's %u rows", max_kv_len, k_stride);
+    if (!q || !k || !v || !o || !kv_len || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(MAKO_EINVAL, "decode: null or unaligned tensor (16-byte alignment)");
+    if (batch == 0)
+        return MAKO_OK;
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    mako::DecodeParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = o;
+    p.kv_len = kv_len;
+    p.len = 0;
+    p.q_bstride = uint64_t(heads) * dim;
+    p.q_hstride = dim;
+    p.k_hstride = uint64_t(k_stride) * dim;
+    p.k_bstride = uint64_t(kv_heads) * p.k_hstride;
+    p.o_bstride = uint64_t(heads) * dim;
+    p.batch = batch;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.scale = 1.0f / sqrtf(float(dim));
+    mako::decode_plan(max_kv_len, batch, kv_heads, heads, ctx->num_sms, &p.chunk, &p.n_splits);
+    void *op, *mlp;
+    if (int rc = scratch(ctx, "dec_o", size_t(batch) * heads * p.n_splits * dim * 4, &op))
+        return rc;
+    if (int rc = scratch(ctx, "dec_ml", size_t(batch) * heads * p.n_splits * 8, &mlp))
+        return rc;
+    p.o_part = static_cast<float*>(op);
+    p.ml_part = static_cast<float2*>(mlp);
+    ctx->launches += 2;
+    return launched("decode", mako::launch_decode(p, dtype, dim, static_cast<cudaStream_t>(stream)));
+}
+
+int mako_cube_select(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, uint32_t heads,
+                     uint32_t q_pad, uint32_t k_pad, uint32_t n_cubes, const uint32_t* cnt, uint32_t topk,
+                     uint16_t** sel, uint16_t** nsel, uint32_t local, uint32_t stride)
+{
+    if (int rc = check_ctx(ctx, dtype))
+        return rc;
+    if (n_cubes > 4096 || !topk || (local != 0 && local != 1 && local != 3))
+        return fail(MAKO_EINVAL, "cube_select: %u cubes, top %u, local %u", n_cubes, topk, local);
+    if (uint64_t(n_cubes) * 64 > q_pad || uint64_t(n_cubes) * 64 > k_pad)
+        return fail(MAKO_EINVAL, "cube_select: %u cubes of 64 rows beyond q_pad %u / k_pad %u", n_cubes, q_pad, k_pad);
+    if (!q || !k || !cnt || !sel || !nsel || !aligned16(q) || !aligned16(k))
+        return fail(MAKO_EINVAL, "cube_select: null or unaligned argument");
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    const uint32_t kk = topk < n_cubes ? topk : n_cubes;
+    mako::CubeParams p{};
+    void *qp, *kp, *sc, *s, *ns;
+    const size_t nc = n_cubes ? n_cubes : 1;
+    if (int rc = scratch(ctx, "c_qp", size_t(heads) * nc * 128 * 4, &qp))
+        return rc;
+    if (int rc = scratch(ctx, "c_kp", size_t(heads) * nc * 128 * 4, &kp))
+        return rc;
+    if (int rc = scratch(ctx, "c_sc", size_t(heads) * nc * nc * 4, &sc))
+        return rc;
+    if (int rc = scratch(ctx, "c_sel", size_t(heads) * nc * (kk ? kk : 1) * 2, &s))
+        return rc;
+    if (int rc = scratch(ctx, "c_nsel", size_t(heads) * nc * 2, &ns))
+        return rc;
+    p.q = q;
+    p.k = k;
+    p.cnt = cnt;
+    p.qp = static_cast<float*>(qp);
+    p.kp = static_cast<float*>(kp);
+    p.sc = static_cast<float*>(sc);
+    p.sel = static_cast<uint16_t*>(s);
+    p.nsel = static_cast<uint16_t*>(ns);
+    p.heads = heads;
+    p.q_pad = q_pad;
+    p.k_pad = k_pad;
+    p.n_cubes = n_cubes;
+    p.topk = topk;
+    p.local = local;
+    p.stride = stride;
+    *sel = p.sel;
+    *nsel = p.nsel;
+    ctx->launches += n_cubes ? 3 : 0;
+    return launched("cube_select", mako::launch_cube_select(p, dtype, static_cast<cudaStream_t>(stream)));
+}
+
+namespace {
+
+int sparse_common(mako_attn_ctx* ctx, void* stream, int dtype, mako::AttnParams& p, bool sel_i32)
+{
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    p.scale = 1.0f / sqrtf(128.0f);
+    ctx->launches += 1;
+    return launched("attention_sparse",
+                    mako::launch_attn_mma(p, dtype, 128, true, sel_i32, static_cast<cudaStream_t>(stream)));
+}
+
+} // namespace
+
+int mako_attention_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v,
+                          float* o, uint32_t n_q, uint32_t q_pad, uint32_t n_k, uint32_t k_pad, uint32_t heads,
+                          uint32_t kv_heads, uint32_t width, uint32_t n_cubes, uint32_t topk, uint32_t dense0,
+                          uint32_t dense1, const uint16_t* sel, const uint16_t* nsel, const uint8_t* valid,
+                          const int32_t* map)
+{
+    if (int rc = check_ctx(ctx, dtype))
+        return rc;
+    if (q_pad % 64 || k_pad % 128 || dense0 % 32)
+        return fail(MAKO_EINVAL, "attention_sparse: q_pad a multiple of 64, k_pad of 128, the dense rows from a "
+                                 "multiple of 32");
+    if (!heads || !kv_heads || heads % kv_heads)
+        return fail(MAKO_EINVAL, "attention_sparse: %u heads over %u kv heads", heads, kv_heads);
+    if (q_pad < n_q || k_pad < n_k || dense0 > dense1 || dense1 > k_pad || uint64_t(n_cubes) * 64 > q_pad ||
+        uint64_t(n_cubes) * 64 > k_pad || width < heads * 128)
+        return fail(MAKO_EINVAL, "attention_sparse: rows n_q %u q_pad %u n_k %u k_pad %u dense [%u, %u) cubes %u width %u",
+                    n_q, q_pad, n_k, k_pad, dense0, dense1, n_cubes, width);
+    if (!q || !k || !v || !o || !valid || !map || (n_cubes && (!sel || !nsel)) || !aligned16(q) || !aligned16(k) ||
+        !aligned16(v) || !aligned16(o))
+        return fail(MAKO_EINVAL, "attention_sparse: null or unaligned argument");
+    if (n_q == 0)
+        return MAKO_OK;
+    mako::AttnParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = o;
+    p.n_q = n_q;
+    p.q_pad = q_pad;
+    p.n_k = n_k;
+    p.k_pad = k_pad;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.width = width;
+    p.n_cubes = n_cubes;
+    p.max_sel = topk < n_cubes ? topk : n_cubes;
+    p.dense0 = dense0;
+    p.dense1 = dense1;
+    p.sel = sel;
+    p.nsel = nsel;
+    p.valid = valid;
+    p.map = map;
+    return sparse_common(ctx, stream, dtype, p, false);
+}
+
+int mako_attention_block_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k,
+                                const void* v, float* o, uint32_t n, uint32_t heads, uint32_t kv_heads,
+                                const int32_t* lists, const int32_t* counts, uint32_t max_list)
+{
+    if (int rc = check_ctx(ctx, dtype))
+        return rc;
+    if (n % 64 || !heads || !kv_heads || heads % kv_heads)
+        return fail(MAKO_EINVAL, "block_sparse: %u rows (a multiple of 64), %u heads over %u kv heads", n, heads,
+                    kv_heads);
+    if (!q || !k || !v || !o || !lists || !counts || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(MAKO_EINVAL, "block_sparse: null or unaligned argument");
+    if (n == 0)
+        return MAKO_OK;
+    mako::AttnParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = o;
+    p.n_q = n;
+    p.q_pad = n;
+    p.n_k = n;
+    p.k_pad = n;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.width = heads * 128;
+    p.n_cubes = n / 64;
+    p.max_sel = max_list;
+    p.dense0 = n;
+    p.dense1 = n;
+    p.sel = lists;
+    p.nsel = counts;
+    p.valid = nullptr;
+    p.map = nullptr;
+    return sparse_common(ctx, stream, dtype, p, true);
+}
+
+} // extern "C"

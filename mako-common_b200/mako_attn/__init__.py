@@ -1,0 +1,162 @@
+"""Python binding of libmako_attn.so (include/mako_attn.h) over torch CUDA tensors.
+
+The library is the product; this module only marshals torch tensors (device memory, the current stream) into the
+C ABI.  It raises if the library is missing or a call fails -- there is no fallback of any kind.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmako_attn.so")
+
+F16, BF16 = 0, 1
+OK, EINVAL, ENOMEM, ECUDA, ENOTSUP = 0, -22, -12, -5, -95
+OPT_PREFILL_KERNEL, OPT_DECODE_ROUTE = 1, 2
+UINT32_MAX = 0xFFFFFFFF
+
+# Every symbol include/mako_attn.h declares, for the load check.
+SYMBOLS = (
+    "mako_attn_last_error", "mako_attn_version", "mako_attn_create", "mako_attn_destroy", "mako_attn_set_option",
+    "mako_attn_launches", "mako_attention", "mako_attention_decode", "mako_cube_select", "mako_attention_sparse",
+    "mako_attention_block_sparse",
+)
+
+_lib = None
+
+
+class MakoError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{msg} (code {code})")
+        self.code = code
+
+
+def lib():
+    """Loads libmako_attn.so and declares its signatures (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C mako-common_b200` (or __graft_entry__.build())")
+    L = ctypes.CDLL(LIB_PATH)
+    u32, i32, i64, p = ctypes.c_uint32, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p
+    L.mako_attn_last_error.restype = ctypes.c_char_p
+    L.mako_attn_last_error.argtypes = []
+    L.mako_attn_version.restype = i32
+    L.mako_attn_create.argtypes = [i32, ctypes.POINTER(p)]
+    L.mako_attn_destroy.argtypes = [p]
+    L.mako_attn_set_option.argtypes = [p, i32, i64]
+    L.mako_attn_launches.argtypes = [p, ctypes.POINTER(ctypes.c_uint64)]
+    L.mako_attention.argtypes = [p, p, i32, p, p, p, p] + [u32] * 10
+    L.mako_attention_decode.argtypes = [p, p, i32, p, p, p, p, u32, p, u32, u32, u32, u32, u32]
+    L.mako_cube_select.argtypes = ([p, p, i32, p, p] + [u32] * 4 + [p, u32, ctypes.POINTER(p), ctypes.POINTER(p)]
+                                   + [u32, u32])
+    L.mako_attention_sparse.argtypes = [p, p, i32, p, p, p, p] + [u32] * 11 + [p, p, p, p]
+    L.mako_attention_block_sparse.argtypes = [p, p, i32, p, p, p, p, u32, u32, u32, p, p, u32]
+    for name in SYMBOLS:
+        if name != "mako_attn_last_error":
+            getattr(L, name).restype = i32
+    _lib = L
+    return L
+
+
+def _check(rc: int):
+    if rc != OK:
+        raise MakoError(rc, lib().mako_attn_last_error().decode())
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    import torch
+    s = torch.cuda.current_stream() if stream is None else stream
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.float16:
+        return F16
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise TypeError(f"16-bit float tensors only, got {t.dtype}")
+
+
+class _DeviceArray:
+    """A raw device allocation described by __cuda_array_interface__ (torch.as_tensor views it without a copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_view(ptr: int, shape, typestr: str = "<i2"):
+    """A torch CUDA tensor over memory the library owns (e.g. cube_select's sel / nsel scratch)."""
+    import torch
+    return torch.as_tensor(_DeviceArray(ptr, shape, typestr), device="cuda")
+
+
+class Context:
+    """One mako_attn_ctx (its scratch and options) on a CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self._h = ctypes.c_void_p()
+        _check(lib().mako_attn_create(device, ctypes.byref(self._h)))
+        self.device = device
+
+    def close(self):
+        if self._h:
+            _check(lib().mako_attn_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_option(self, option: int, value: int):
+        _check(lib().mako_attn_set_option(self._h, option, value))
+
+    def launches(self) -> int:
+        n = ctypes.c_uint64()
+        _check(lib().mako_attn_launches(self._h, ctypes.byref(n)))
+        return n.value
+
+    # -- TransformerRuntime::attention (src/models/runtime.cpp:262-273)
+    def attention(self, q, k, v, o, n_q, q_pad, n_k, k_pad, heads, kv_heads, q_pos0=0, block=UINT32_MAX, dim=128,
+                  width=0, stream=None):
+        _check(lib().mako_attention(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(o), n_q,
+                                    q_pad, n_k, k_pad, heads, kv_heads, q_pos0, block & UINT32_MAX, dim, width))
+
+    def attention_decode(self, q, k, v, o, kv_len, max_kv_len, heads, kv_heads, dim, k_stride, stream=None):
+        batch = kv_len.numel()
+        _check(lib().mako_attention_decode(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                           batch, _ptr(kv_len), max_kv_len, heads, kv_heads, dim, k_stride))
+
+    # -- TransformerRuntime::cube_select (src/models/runtime.cpp:286-303); returns (sel, nsel) as int16 tensor views
+    # of the context's scratch ([heads][n_cubes][min(topk, n_cubes)] and [heads][n_cubes], uint16 bit patterns),
+    # valid until the next cube_select on this context.
+    def cube_select(self, q, k, heads, q_pad, k_pad, n_cubes, cnt, topk, local=0, stride=0, stream=None):
+        sel, nsel = ctypes.c_void_p(), ctypes.c_void_p()
+        _check(lib().mako_cube_select(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k), heads, q_pad, k_pad,
+                                      n_cubes, _ptr(cnt), topk, ctypes.byref(sel), ctypes.byref(nsel), local, stride))
+        kk = min(topk, n_cubes)
+        return device_view(sel.value, (heads, n_cubes, kk)), device_view(nsel.value, (heads, n_cubes))
+
+    # -- TransformerRuntime::attention_sparse (src/models/runtime.cpp:305-317); sel/nsel as tensors or raw pointers
+    def attention_sparse(self, q, k, v, o, n_q, q_pad, n_k, k_pad, heads, kv_heads, width, n_cubes, topk, dense0,
+                         dense1, sel, nsel, valid, map_, stream=None):
+        sp = sel if isinstance(sel, int) or sel is None else sel.data_ptr()
+        np_ = nsel if isinstance(nsel, int) or nsel is None else nsel.data_ptr()
+        _check(lib().mako_attention_sparse(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                           n_q, q_pad, n_k, k_pad, heads, kv_heads, width, n_cubes, topk, dense0,
+                                           dense1, ctypes.c_void_p(sp), ctypes.c_void_p(np_), _ptr(valid), _ptr(map_)))
+
+    def attention_block_sparse(self, q, k, v, o, n, heads, kv_heads, lists, counts, stream=None):
+        _check(lib().mako_attention_block_sparse(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k), _ptr(v),
+                                                 _ptr(o), n, heads, kv_heads, _ptr(lists), _ptr(counts),
+                                                 lists.shape[-1]))

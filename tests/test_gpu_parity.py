@@ -1,0 +1,235 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle on the same seeded inputs.
+
+Tolerance: max-abs <= 2e-3 and relative L2 <= 1e-3 against the double-accumulated oracle,
+plus the reference test's worst-row relative L2 < 5e-3 (tests/sparse_attn_test.cpp:181).  Index and mask handling
+is exact: cube selections bit for bit, rows outside the output untouched (sentinel 12345,
+tests/sparse_attn_test.cpp:86,138-141,182).
+"""
+import numpy as np
+import pytest
+
+import attn_cases as C
+
+pytestmark = pytest.mark.gpu
+SENTINEL = 12345.0
+
+
+def dev(bits, dtype):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16))
+    return t.view(torch.bfloat16 if dtype == 1 else torch.float16).cuda()
+
+
+def dev_raw(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def run_dense(ctx, case, kernel=0):
+    import torch
+    import mako_attn
+    ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, kernel)
+    q, k, v = dev(case["q"], case["dtype"]), dev(case["k"], case["dtype"]), dev(case["v"], case["dtype"])
+    width = case["heads"] * case["dim"]
+    o = torch.full((case["q_pad"], width), SENTINEL, dtype=torch.float32, device="cuda")
+    ctx.attention(q, k, v, o, case["n_q"], case["q_pad"], case["n_k"], case["k_pad"], case["heads"], case["kv_heads"],
+                  case["q_pos0"], case["block"], case["dim"])
+    torch.cuda.synchronize()
+    return o.cpu().numpy()
+
+
+def oracle_dense(oracle, case, rows=None):
+    return oracle.attention(case["dtype"], case["q"], case["k"], case["v"], case["n_q"], case["q_pad"], case["n_k"],
+                            case["k_pad"], case["heads"], case["kv_heads"], case["q_pos0"], case["block"], case["dim"],
+                            rows=rows)
+
+
+DENSE = [
+    # config 1 exactly: causal GQA prefill fp16, B1 H16/8 D128 S512, seed 0
+    ("config1", dict(seed=0, heads=16, kv_heads=8, dim=128, n_q=512, n_k=512, dtype=0)),
+    ("config1-bf16", dict(seed=0, heads=16, kv_heads=8, dim=128, n_q=512, n_k=512, dtype=1)),
+    ("ragged-causal", dict(seed=1, heads=4, kv_heads=4, dim=128, n_q=333, n_k=333, dtype=0)),
+    ("bidir-gqa", dict(seed=2, heads=8, kv_heads=2, dim=128, n_q=200, n_k=450, block=0, dtype=1)),
+    ("block-mask", dict(seed=3, heads=4, kv_heads=2, dim=128, n_q=300, n_k=300, block=77, dtype=0)),
+    ("q-offset", dict(seed=4, heads=4, kv_heads=1, dim=128, n_q=70, n_k=600, q_pos0=530, dtype=0)),
+    ("d64", dict(seed=5, heads=6, kv_heads=3, dim=64, n_q=257, n_k=257, dtype=0)),
+    ("d64-bidir-bf16", dict(seed=6, heads=2, kv_heads=2, dim=64, n_q=130, n_k=130, block=0, dtype=1)),
+    ("d256", dict(seed=7, heads=4, kv_heads=2, dim=256, n_q=190, n_k=190, dtype=0)),
+    ("d256-bf16", dict(seed=8, heads=2, kv_heads=1, dim=256, n_q=64, n_k=300, block=0, dtype=1)),
+    ("video-rms", dict(seed=9, heads=2, kv_heads=2, dim=128, n_q=1000, n_k=1000, block=0, dtype=1, qk_rms_norm=True)),
+    ("config3-scale", dict(seed=10, heads=4, kv_heads=1, dim=128, n_q=700, n_k=700, dtype=1, scale=0.5)),
+]
+
+
+@pytest.mark.parametrize("name,kw", DENSE, ids=[n for n, _ in DENSE])
+@pytest.mark.parametrize("kernel", [0, 1])
+def test_dense(ctx, oracle, name, kw, kernel):
+    case = C.dense_case(**kw)
+    got = run_dense(ctx, case, kernel)
+    want = oracle_dense(oracle, case)
+    ok, stats = C.within(got[:case["n_q"]], want)
+    assert ok, f"{name}: max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+    assert np.all(got[case["n_q"]:] == SENTINEL), "rows past n_q were written"
+
+
+def test_dense_no_keys_gives_zeros(ctx, oracle):
+    case = C.dense_case(seed=12, heads=2, kv_heads=2, dim=128, n_q=64, n_k=0, dtype=0)
+    got = run_dense(ctx, case)
+    assert np.all(got[:64] == 0.0)
+
+
+def test_single_query_routes_to_decode(ctx, oracle):
+    import mako_attn
+    for q_pos0, block in ((799, C.UINT32_MAX), (300, C.UINT32_MAX), (10, 5), (0, 0)):
+        case = C.dense_case(seed=13, heads=8, kv_heads=2, dim=128, n_q=1, n_k=800, q_pos0=q_pos0, block=block,
+                            dtype=0)
+        got = run_dense(ctx, case)
+        want = oracle_dense(oracle, case)
+        ok, stats = C.within(got[:1], want)
+        assert ok, f"pos {q_pos0} block {block}: {stats}"
+        ctx.set_option(mako_attn.OPT_DECODE_ROUTE, 0)
+        got2 = run_dense(ctx, case)
+        ctx.set_option(mako_attn.OPT_DECODE_ROUTE, 1)
+        ok, stats = C.within(got2[:1], want)
+        assert ok, f"prefill kernel at n_q 1: {stats}"
+
+
+def run_decode(ctx, case, max_len=None):
+    import torch
+    d = case["dtype"]
+    q, k, v = dev(case["q"], d), dev(case["k"], d), dev(case["v"], d)
+    lens = dev_raw(case["kv_len"])
+    batch = lens.numel()
+    o = torch.full((batch, case["heads"] * case["dim"]), SENTINEL, dtype=torch.float32, device="cuda")
+    ctx.attention_decode(q, k, v, o, lens, int(case["kv_len"].max()) if max_len is None else max_len, case["heads"],
+                         case["kv_heads"], case["dim"], case["k_stride"])
+    torch.cuda.synchronize()
+    return o.cpu().numpy()
+
+
+DECODE = [
+    ("config2-short", dict(seed=20, batch=8, heads=32, kv_heads=8, dim=128, lo=1000, hi=3000, dtype=0)),
+    ("config2", dict(seed=21, batch=8, heads=32, kv_heads=8, dim=128, lo=16384, hi=32768, dtype=0)),
+    ("ragged-tiny", dict(seed=22, batch=5, heads=4, kv_heads=4, dim=128, lo=1, hi=70, dtype=0)),
+    ("bf16-gqa", dict(seed=23, batch=3, heads=16, kv_heads=2, dim=128, lo=500, hi=5000, dtype=1)),
+    ("d64", dict(seed=24, batch=2, heads=8, kv_heads=1, dim=64, lo=100, hi=2000, dtype=0)),
+    ("d256", dict(seed=25, batch=2, heads=4, kv_heads=2, dim=256, lo=100, hi=2000, dtype=1)),
+    ("group32", dict(seed=26, batch=2, heads=32, kv_heads=1, dim=128, lo=300, hi=900, dtype=0)),
+]
+
+
+@pytest.mark.parametrize("name,kw", DECODE, ids=[n for n, _ in DECODE])
+def test_decode(ctx, oracle, name, kw):
+    case = C.decode_case(**kw)
+    got = run_decode(ctx, case)
+    want = oracle.decode(case["dtype"], case["q"], case["k"], case["v"], case["kv_len"], case["heads"],
+                         case["kv_heads"], case["dim"], case["k_stride"])
+    ok, stats = C.within(got, want)
+    assert ok, f"{name}: max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+
+
+def test_decode_zero_length_gives_zeros(ctx, oracle):
+    case = C.decode_case(seed=27, batch=3, heads=4, kv_heads=2, dim=128, lo=10, hi=20, dtype=0)
+    case["kv_len"][1] = 0
+    got = run_decode(ctx, case)
+    assert np.all(got[1] == 0.0)
+    want = oracle.decode(0, case["q"], case["k"], case["v"], case["kv_len"], 4, 2, 128, case["k_stride"])
+    assert C.within(got, want)[0]
+
+
+def sparse_fixture_run(ctx, oracle, dtype=0, topk=3, local=0, stride=0):
+    import torch
+    fx = oracle.sparse_test_fixture()
+    q, k, v = dev(fx["q"], dtype), dev(fx["k"], dtype), dev(fx["v"], dtype)
+    cnt = dev_raw(fx["cnt"])
+    valid, map_ = dev_raw(fx["valid"]), dev_raw(fx["map"])
+    sel_t, nsel_t = ctx.cube_select(q, k, 2, 448, 512, 6, cnt, topk, local, stride)
+    o = torch.full((448, 256), SENTINEL, dtype=torch.float32, device="cuda")
+    ctx.attention_sparse(q, k, v, o, 444, 448, 444, 512, 2, 2, 256, 6, topk, 384, 444, sel_t, nsel_t, valid, map_)
+    torch.cuda.synchronize()
+    sel = sel_t.cpu().numpy().view(np.uint16)
+    nsel = nsel_t.cpu().numpy().view(np.uint16)
+    return fx, sel, nsel, o.cpu().numpy()
+
+
+def test_sparse_reference_fixture(ctx, oracle):
+    """tests/sparse_attn_test.cpp re-run through the C ABI: selection exact (vs the fp32 restatement and the
+    reference's double procedure), attention within tolerance, unmapped rows untouched."""
+    fx, sel, nsel, o = sparse_fixture_run(ctx, oracle)
+    want_sel, want_nsel, *_ = oracle.cube_select(0, fx["q"], fx["k"], 2, 448, 512, 6, fx["cnt"], 3, mode=1)
+    dbl_sel, *_ = oracle.cube_select(0, fx["q"], fx["k"], 2, 448, 512, 6, fx["cnt"], 3, mode=0)
+    np.testing.assert_array_equal(sel, want_sel)
+    np.testing.assert_array_equal(sel, dbl_sel)
+    np.testing.assert_array_equal(nsel, want_nsel)
+    want = np.full((448, 256), SENTINEL, np.float32)
+    oracle.attention_sparse(0, fx["q"], fx["k"], fx["v"], 444, 448, 444, 512, 2, 2, 256, 6, 3, 384, 444, sel, nsel,
+                            fx["valid"], fx["map"], out=want)
+    mapped = np.array([r for r in range(444) if fx["map"][r] >= 0])
+    ok, stats = C.within(o[mapped], want[mapped])
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+    untouched = [r for r in range(448) if r >= 444 or fx["map"][r] < 0]
+    assert np.all(o[untouched] == SENTINEL)
+
+
+def test_sparse_local_cubes(ctx, oracle):
+    fx, sel, nsel, _ = sparse_fixture_run(ctx, oracle, topk=4, local=3, stride=1)
+    want, *_ = oracle.cube_select(0, fx["q"], fx["k"], 2, 448, 512, 6, fx["cnt"], 4, local=3, stride=1)
+    np.testing.assert_array_equal(sel, want)
+
+
+def test_cube_select_large_bit_exact(ctx, oracle):
+    """Many cubes, partial cubes, bf16: the selection equals the fp32 restatement bit for bit."""
+    import torch
+    rng = np.random.default_rng(30)
+    heads, n_cubes, topk = 3, 300, 40
+    n = n_cubes * 64
+    cnt = rng.integers(1, 65, size=n_cubes).astype(np.uint32)
+    cnt[::7] = 64
+    valid = np.zeros(n, np.uint8)
+    for c in range(n_cubes):
+        valid[c * 64:c * 64 + cnt[c]] = 1
+    for dtype in (0, 1):
+        x = C.normal(rng, (2, heads, n, 128)) * valid[None, None, :, None]
+        q, k = oracle.to_bits(x[0], dtype), oracle.to_bits(x[1], dtype)
+        sel_t, _ = ctx.cube_select(dev(q, dtype), dev(k, dtype), heads, n, n, n_cubes, dev_raw(cnt), topk, 1, 0)
+        torch.cuda.synchronize()
+        sel = sel_t.cpu().numpy().view(np.uint16)
+        want, *_ = oracle.cube_select(dtype, q, k, heads, n, n, n_cubes, cnt, topk, local=1, mode=1)
+        np.testing.assert_array_equal(sel, want)
+
+
+def test_block_sparse_lists(ctx, oracle):
+    """Config 4's mask format (int32 sorted kept-block lists + counts) at a reduced length."""
+    import torch
+    heads, n, dtype = 4, 2048, 1
+    nb = n // 64
+    lists, counts = C.block_lists(40, heads, nb, 0.15)
+    counts[1, 3] = 0  # a query block that keeps nothing: zeros
+    case = C.dense_case(seed=41, heads=heads, kv_heads=heads, dim=128, n_q=n, n_k=n, dtype=dtype)
+    q, k, v = dev(case["q"], dtype), dev(case["k"], dtype), dev(case["v"], dtype)
+    o = torch.full((n, heads * 128), SENTINEL, dtype=torch.float32, device="cuda")
+    ctx.attention_block_sparse(q, k, v, o, n, heads, heads, dev_raw(lists), dev_raw(counts))
+    torch.cuda.synchronize()
+    got = o.cpu().numpy()
+    want = oracle.attention_sparse(dtype, case["q"], case["k"], case["v"], n, case["q_pad"], n, case["k_pad"], heads,
+                                   heads, heads * 128, nb, lists.shape[-1], n, n, lists.astype(np.uint16),
+                                   counts.astype(np.uint16), np.ones(case["k_pad"], np.uint8),
+                                   np.arange(case["q_pad"], dtype=np.int32))[:n]
+    ok, stats = C.within(got, want)
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+    assert np.all(got[3 * 64:4 * 64, 128:256] == 0.0)
+
+
+def test_argument_errors(ctx):
+    import torch
+    import mako_attn
+    q = torch.zeros(64 * 128, dtype=torch.float16, device="cuda")
+    o = torch.zeros(64 * 128, dtype=torch.float32, device="cuda")
+    with pytest.raises(mako_attn.MakoError, match="heads of 96"):
+        ctx.attention(q, q, q, o, 10, 64, 10, 64, 1, 1, 0, 0, 96)
+    with pytest.raises(mako_attn.MakoError, match="q_pad"):
+        ctx.attention(q, q, q, o, 10, 32, 10, 64, 1, 1, 0, 0, 128)
+    with pytest.raises(mako_attn.MakoError, match="cube_select"):
+        ctx.cube_select(q, q, 1, 64, 128, 5000, o, 3)
+    with pytest.raises(mako_attn.MakoError, match="multiple of 64"):
+        ctx.attention_sparse(q, q, q, o, 10, 60, 10, 128, 1, 1, 128, 0, 1, 0, 10, None, None, o, o)
