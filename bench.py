@@ -21,12 +21,9 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -302,52 +299,57 @@ def make_workload(name):
 # ---- clocks ---------------------------------------------------------------------------------------------------------
 
 class Clocks:
-    """nvidia-smi sampled every 200 ms during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled through NVML every 5 ms by a background thread; the summary keeps the
+    samples taken between mark_start() and mark_stop() (the timed region), else all of them."""
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, index):
-        self.index = index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.p = None
+        import threading
+        self.samples, self.window, self.ok = [], [None, None], False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: reported, the run continues
+            self.err = str(e)
+        self.stop_flag = threading.Event()
+        self.t = threading.Thread(target=self._loop, daemon=True)
+
+    def _loop(self):
+        while not self.stop_flag.is_set():
+            try:
+                sm = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((time.perf_counter(), sm, rs))
+            except Exception:
+                pass
+            time.sleep(0.005)
 
     def start(self):
-        try:
-            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
-                                      stderr=subprocess.DEVNULL)
-        except Exception:
-            self.p = None
+        if self.ok:
+            self.t.start()
+
+    def mark_start(self):
+        self.window[0] = time.perf_counter()
+
+    def mark_stop(self):
+        self.window[1] = time.perf_counter()
 
     def stop(self):
-        if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
-        self.p.terminate()
-        try:
-            self.p.wait(timeout=5)
-        except Exception:
-            self.p.kill()
-        self.f.flush()
-        self.f.seek(0)
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.f.read().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for n, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(n)
-        os.unlink(self.f.name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"nvml unavailable: {self.err}"]}
+        self.stop_flag.set()
+        self.t.join(timeout=1)
+        t0, t1 = self.window
+        inside = [s for s in self.samples if t0 is not None and t1 is not None and t0 <= s[0] <= t1]
+        use = inside or self.samples
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(s[2] & bit for s in use))
+        return {"sm_mhz": statistics.median(s[1] for s in use) if use else None, "sm_max_mhz": self.max_sm,
+                "reasons": reasons, "samples": len(use),
+                "window": "timed region" if inside else "whole run (timed region shorter than one sample)"}
 
 
 # ---- runs -----------------------------------------------------------------------------------------------------------
@@ -410,14 +412,15 @@ def run_mako(args):
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE)
     stream = torch.cuda.current_stream()
 
+    clocks = Clocks(local)
+    clocks.start()
     for _ in range(args.warmup):
         W.step(ctx)
     barrier(world)
     launches0 = ctx.launches()
-    clocks = Clocks(torch.cuda.current_device())
-    clocks.start()
     times = []
     barrier(world)
+    clocks.mark_start()
     for _ in range(args.steps):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -426,7 +429,7 @@ def run_mako(args):
         e1.record(stream)
         times.append((e0, e1))
     barrier(world)
-    clk = clocks.stop()
+    clocks.mark_stop()
     launches = ctx.launches() - launches0
     ms = [a.elapsed_time(b) for a, b in times]
     total_ms = max_over_ranks(sum(ms), world)
@@ -456,6 +459,7 @@ def run_mako(args):
             e2e_times.append((e0, e1))
     barrier(world)
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_times), world) / args.steps
+    clk = clocks.stop()
     e2e_value = W.to_metric(work * world / (e2e_ms / 1e3))
 
     hbm, tflops, src = peaks()

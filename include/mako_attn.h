@@ -58,6 +58,10 @@ int mako_attn_set_option(mako_attn_ctx* ctx, int option, int64_t value);
 /* Kernel launches this context has enqueued since it was created (a counter for profiling harnesses; the
  * reference's equivalent is its per-kernel telemetry, src/gpu/runtime.cpp:343-370). */
 int mako_attn_launches(mako_attn_ctx* ctx, uint64_t* out);
+/* Reads and clears the context's device error flag (synchronising the device): nonzero when a pipelined kernel gave
+ * up on a wait (its bounded spin ran out) and left its outputs incomplete.  No reference counterpart: the reference
+ * learns of a failed command buffer in gpu::Runtime::finish (src/gpu/runtime.cpp:466-471). */
+int mako_attn_device_error(mako_attn_ctx* ctx, int* out);
 
 /* Flash attention over 16-bit head tiles: q [heads][q_pad][dim], k and v [kv_heads][k_pad][dim] into
  * o [n_q][width] floats, head h at column h * dim and reading kv head h / (heads / kv_heads).  Key j is visible to

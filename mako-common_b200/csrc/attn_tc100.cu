@@ -1,0 +1,487 @@
+// Flash attention for 128-wide heads on sm_100a tensor cores (tcgen05 UMMA, TMEM accumulators, TMA-fed shared
+// memory): the dense masked form of TransformerRuntime::attention (src/models/runtime.cpp:262-273; maths of
+// flash_attn_coop, src/kernels/ops.metal:230-363).
+//
+// A CTA owns 256 query rows of one head as two 128-row tiles A and B that share every K / V tile (half the K / V
+// reads of one tile per CTA).  Warp roles (384 threads):
+//   warp 0        TMA producer: Q once, then 128-key K and V tiles into two-stage rings (128-byte swizzle).
+//   warp 1        UMMA issuer (one thread) and TMEM owner: S_X = Q_X K^T (SS, M 128 N 128), O_X += P_X V (TS, P from
+//                 TMEM, V MN-major from shared memory).
+//   warps 4-7     softmax of tile A, warps 8-11 softmax of tile B: thread r owns query row r = TMEM lane r, so a
+//                 row's 128 scores sit in one thread's registers (no shuffles).  Base-2 online softmax with the
+//                 reference's lazy rescale (a row's maximum moves only when a score passes it by 8, so P <= 256 fits
+//                 fp16; ops.metal:303-316); P goes back into S's TMEM columns as fp16 pairs for the P.V product.
+// TMEM (512 columns): S_A 0-127, S_B 128-255, O_A 256-383, O_B 384-511.  The issue order per key tile is
+// PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1) -- while one tile's softmax runs the tensor core works on the other's.
+// QK_X(j+1) is issued after PV_X(j) completes (it overwrites the P that PV_X(j) reads).
+//
+// P.V runs in fp16: for fp16 inputs V is used as it is; for bf16 inputs a pre-pass writes V * 2^k per kv head into
+// an fp16 copy (k puts the head's largest |v| in [2^14, 2^15), exact for every value above 2^-28 of that maximum) and
+// the epilogue multiplies by 2^-k.  P in fp16 costs ~2^-11 relative error where bf16 P would cost 2^-8.
+//
+// Every mbarrier wait is bounded (clock64); on a timeout the thread records an error code in p.err, waits (bounded)
+// for its own copies / MMAs in flight, and the CTA frees its TMEM and returns.
+#include "common.cuh"
+#include "kernels.h"
+#include "tc100.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace mako {
+namespace {
+
+using namespace tc;
+
+constexpr int TD = 128, TBM = 128, TBN = 128, TNS = 2, TNT = 384;
+constexpr uint32_t BOX_BYTES = 128 * 64 * 2;   // one TMA box: 128 rows x 64 16-bit values
+constexpr uint32_t TILE_BYTES = 2 * BOX_BYTES;  // 128 rows x 128 values
+constexpr uint32_t SMEM_Q = 0, SMEM_K = 2 * TILE_BYTES, SMEM_V = SMEM_K + TNS * TILE_BYTES;
+constexpr uint32_t SMEM_BAR = SMEM_V + TNS * TILE_BYTES;
+constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 256 + 1024;  // + barriers + alignment slack
+constexpr long long WAIT_LIMIT = 1ll << 31;             // clock cycles (~1 s) before a wait gives up
+
+struct __align__(64) TcParams {
+    CUtensorMap tq, tk, tv;
+    float* o;
+    int* err;
+    const float* vinv;  // per kv head: 1 / (the fp16 copy's scale), null for fp16 inputs
+    uint32_t qk_fmt;    // Q / K element format: 0 fp16, 1 bf16
+    uint32_t n_q, q_pad, n_k, k_pad, heads, kv_heads, q_pos0, block, width, n_tiles;
+    float scale_log2;
+};
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
+{
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__ TcParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    const uint32_t sQ = base + SMEM_Q, sK = base + SMEM_K, sV = base + SMEM_V, sB = base + SMEM_BAR;
+    // barriers
+    const uint32_t q_full = sB;
+    auto k_full = [&](uint32_t s) { return sB + 8 + 8 * s; };
+    auto k_empty = [&](uint32_t s) { return sB + 24 + 8 * s; };
+    auto v_full = [&](uint32_t s) { return sB + 40 + 8 * s; };
+    auto v_empty = [&](uint32_t s) { return sB + 56 + 8 * s; };
+    auto s_full = [&](uint32_t x) { return sB + 72 + 8 * x; };
+    auto p_full = [&](uint32_t x) { return sB + 88 + 8 * x; };
+    auto pv_done = [&](uint32_t x) { return sB + 104 + 8 * x; };
+    const uint32_t mma_done = sB + 120;
+    const uint32_t tmem_slot = sB + 128;
+    volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t tile = p.n_tiles - 1 - blockIdx.x;  // the longest causal rows first
+    const uint32_t h = blockIdx.y, q0 = tile * 2 * TBM;
+    if (q0 >= p.n_q)
+        return;
+    const uint32_t kvh = h / (p.heads / p.kv_heads);
+    const uint32_t last = p.q_pos0 + min(q0 + 2 * TBM, p.n_q) - 1;
+    const uint32_t n_keys = last >= p.block ? p.n_k : min(p.n_k, last + 1);
+    const uint32_t nb = (n_keys + TBN - 1) / TBN;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (uint32_t s = 0; s < TNS; ++s) {
+            mbar_init(k_full(s), 1);
+            mbar_init(k_empty(s), 1);
+            mbar_init(v_full(s), 1);
+            mbar_init(v_empty(s), 1);
+        }
+        for (uint32_t x = 0; x < 2; ++x) {
+            mbar_init(s_full(x), 1);
+            mbar_init(p_full(x), 128);
+            mbar_init(pv_done(x), 1);
+        }
+        mbar_init(mma_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot_ptr;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            tma_prefetch_desc(&p.tq);
+            tma_prefetch_desc(&p.tk);
+            tma_prefetch_desc(&p.tv);
+            bool ok = true;
+            mbar_expect_tx(q_full, 2 * TILE_BYTES);
+            for (int x = 0; x < 2; ++x)
+                for (int half = 0; half < 2; ++half)
+                    tma_load_3d(sQ + x * TILE_BYTES + half * BOX_BYTES, &p.tq, q_full, half * 64, q0 + x * TBM, h);
+            uint32_t issued = 0;
+            for (uint32_t j = 0; j < nb && ok; ++j) {
+                const uint32_t s = j % TNS, ph = (j / TNS) & 1;
+                if (j >= TNS && !mbar_wait(k_empty(s), ph ^ 1, WAIT_LIMIT)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(k_full(s), TILE_BYTES);
+                for (int half = 0; half < 2; ++half)
+                    tma_load_3d(sK + s * TILE_BYTES + half * BOX_BYTES, &p.tk, k_full(s), half * 64, j * TBN, kvh);
+                if (j >= TNS && !mbar_wait(v_empty(s), ph ^ 1, WAIT_LIMIT)) {
+                    ok = false;
+                    issued = 2 * j + 1;
+                    break;
+                }
+                mbar_expect_tx(v_full(s), TILE_BYTES);
+                for (int half = 0; half < 2; ++half)
+                    tma_load_3d(sV + s * TILE_BYTES + half * BOX_BYTES, &p.tv, v_full(s), half * 64, j * TBN, kvh);
+                issued = 2 * (j + 1);
+            }
+            if (!ok)
+                atomicExch(p.err, 1);
+            // Our copies in flight land before the CTA leaves (already so on the normal path).
+            mbar_wait(q_full, 0, WAIT_LIMIT);
+            for (uint32_t i = issued > 2 * TNS ? issued - 2 * TNS : 0; i < issued; ++i) {
+                const uint32_t j = i / 2, s = j % TNS, ph = (j / TNS) & 1;
+                mbar_wait((i & 1) ? v_full(s) : k_full(s), ph, WAIT_LIMIT);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- UMMA issuer ----------------
+        if (lane == 0 && nb > 0) {
+            const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, TBM, TBN);
+            const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, TBM, TD);
+            bool ok = mbar_wait(q_full, 0, WAIT_LIMIT);
+            auto qk = [&](uint32_t x, uint32_t stage) {
+#pragma unroll
+                for (uint32_t ks = 0; ks < TD / 16; ++ks) {
+                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
+                    umma_ss(tmem + x * 128, sdesc(sQ + x * TILE_BYTES + off, 16, 1024),
+                            sdesc(sK + stage * TILE_BYTES + off, 16, 1024), idesc_qk, ks > 0);
+                }
+            };
+            auto pv = [&](uint32_t x, uint32_t stage, bool acc) {
+#pragma unroll
+                for (uint32_t kk = 0; kk < TBN / 16; ++kk)
+                    umma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
+                            sdesc(sV + stage * TILE_BYTES + kk * 2048, BOX_BYTES, 1024), idesc_pv, acc || kk > 0);
+            };
+            if (ok && (ok = mbar_wait(k_full(0), 0, WAIT_LIMIT))) {
+                fence_after();
+                qk(0, 0);
+                umma_commit(s_full(0));
+                qk(1, 0);
+                umma_commit(s_full(1));
+                umma_commit(k_empty(0));
+            }
+            for (uint32_t j = 0; j < nb && ok; ++j) {
+                const uint32_t s = j % TNS, ph = (j / TNS) & 1;
+                const bool nxt = j + 1 < nb;
+                const uint32_t s1 = (j + 1) % TNS, ph1 = ((j + 1) / TNS) & 1;
+                // tile A
+                if (!(ok = mbar_wait(p_full(0), j & 1, WAIT_LIMIT) && mbar_wait(v_full(s), ph, WAIT_LIMIT)))
+                    break;
+                fence_after();
+                pv(0, s, j > 0);
+                umma_commit(pv_done(0));
+                if (nxt) {
+                    if (!(ok = mbar_wait(k_full(s1), ph1, WAIT_LIMIT) && mbar_wait(pv_done(0), j & 1, WAIT_LIMIT)))
+                        break;
+                    fence_after();
+                    qk(0, s1);
+                    umma_commit(s_full(0));
+                }
+                // tile B
+                if (!(ok = mbar_wait(p_full(1), j & 1, WAIT_LIMIT)))
+                    break;
+                fence_after();
+                pv(1, s, j > 0);
+                umma_commit(pv_done(1));
+                umma_commit(v_empty(s));
+                if (nxt) {
+                    if (!(ok = mbar_wait(pv_done(1), j & 1, WAIT_LIMIT)))
+                        break;
+                    fence_after();
+                    qk(1, s1);
+                    umma_commit(s_full(1));
+                    umma_commit(k_empty(s1));
+                }
+            }
+            if (!ok)
+                atomicExch(p.err, 2);
+            umma_commit(mma_done);  // every MMA issued above has finished before TMEM is freed
+            mbar_wait(mma_done, 0, WAIT_LIMIT);
+        }
+    } else if (warp >= 4) {
+        // ---------------- softmax (and epilogue) of tile X ----------------
+        const uint32_t x = (warp - 4) >> 2, ql = (warp & 3) * 32, row = ql + lane;
+        const uint32_t tl = tmem + (ql << 16);
+        const uint32_t colS = x * 128, colO = 256 + x * 128;
+        const uint32_t pos = p.q_pos0 + q0 + x * TBM + row;
+        const uint32_t lim = pos >= p.block ? p.n_k : min(p.n_k, pos + 1);  // this row sees keys [0, lim)
+        const uint32_t pos1 = p.q_pos0 + q0 + x * TBM;
+        const uint32_t lim1 = pos1 >= p.block ? p.n_k : min(p.n_k, pos1 + 1);  // the tile's first row
+        const float scale = p.scale_log2;
+        float m = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (uint32_t j = 0; j < nb; ++j) {
+            ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), j & 1, WAIT_LIMIT));
+            if (!ok)
+                break;
+            fence_after();
+            uint32_t r[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                tmem_ld32(tl + colS + c * 32, r[c]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                reg_fence(r[c]);
+            const uint32_t j0 = j * TBN;
+            const bool plain = j0 + TBN <= lim1;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < TBN; ++c) {
+                float v = __uint_as_float(r[c >> 5][c & 31]) * scale;
+                if (!plain && j0 + c >= lim)
+                    v = -INFINITY;
+                r[c >> 5][c & 31] = __float_as_uint(v);
+                mx = fmaxf(mx, v);
+            }
+            float f = 1.0f;
+            bool resc = false;
+            if (mx > m + 8.0f) {
+                f = m == -INFINITY ? 0.0f : ex2(m - mx);
+                m = mx;
+                l *= f;
+                resc = true;
+            }
+            uint32_t pk[2][32];
+            float sum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < TBN / 2; ++c) {
+                const float a = m == -INFINITY ? 0.0f : ex2(__uint_as_float(r[(2 * c) >> 5][(2 * c) & 31]) - m);
+                const float b = m == -INFINITY ? 0.0f : ex2(__uint_as_float(r[(2 * c + 1) >> 5][(2 * c + 1) & 31]) - m);
+                sum += a + b;
+                pk[c >> 5][c & 31] = pack_half2(a, b);
+            }
+            l += sum;
+            tmem_st32(tl + colS, pk[0]);
+            tmem_st32(tl + colS + 32, pk[1]);
+            // Rescale this tile's O before P.V adds to it (PV_X(j-1) finished before QK_X(j) was issued).
+            if (__any_sync(0xffffffffu, resc && j > 0)) {
+                const float g = resc ? f : 1.0f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(tl + colO + c * 32, o);
+                    tmem_wait_ld();
+                    reg_fence(o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        o[i] = __float_as_uint(__uint_as_float(o[i]) * g);
+                    tmem_st32(tl + colO + c * 32, o);
+                }
+            }
+            tmem_wait_st();
+            fence_before();
+            mbar_arrive(p_full(x));
+        }
+        if (ok && nb > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(pv_done(x), (nb - 1) & 1, WAIT_LIMIT));
+            fence_after();
+        }
+        if (!ok && lane == 0)
+            atomicExch(p.err, 3);
+        const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
+        const uint32_t grow = q0 + x * TBM + row;
+        float* orow = p.o + uint64_t(grow) * p.width + uint64_t(h) * TD;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            if (ok && nb > 0) {
+                tmem_ld32(tl + colO + c * 32, o);
+                tmem_wait_ld();
+                reg_fence(o);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    o[i] = 0u;
+            }
+            if (grow < p.n_q) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    *reinterpret_cast<float4*>(orow + c * 32 + i * 4) =
+                        make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                    __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+            }
+        }
+    }
+    __syncwarp();
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---- bf16 V -> scaled fp16 copy -----------------------------------------------------------------------------------
+
+// vmax[kvh] = max |v| over the rows that can be attended (rows < n_rows with valid[row] != 0), as float bits.
+__global__ void __launch_bounds__(256) vmax_kernel(const __nv_bfloat16* v, uint32_t* vmax, uint32_t k_pad,
+                                                   uint32_t n_rows, const uint8_t* valid)
+{
+    const uint32_t kvh = blockIdx.y;
+    const uint4* src = reinterpret_cast<const uint4*>(v + uint64_t(kvh) * k_pad * TD);
+    const uint64_t chunks = uint64_t(n_rows) * (TD / 8);
+    uint32_t best = 0;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < chunks; i += uint64_t(gridDim.x) * blockDim.x) {
+        if (valid && !valid[i / (TD / 8)])
+            continue;
+        const uint4 w = src[i];
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            best = max(best, (words[k] & 0x7FFFu) << 16);
+            best = max(best, (words[k] >> 16 & 0x7FFFu) << 16);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0 && best)
+        atomicMax(vmax + kvh, best);
+}
+
+// The power of two that puts `bits` (a float's bits, |v|max) in [2^14, 2^15), and its inverse; 1 for 0 / inf / nan.
+__device__ __forceinline__ void v_scale(uint32_t bits, float& s, float& inv)
+{
+    const int ex = int(bits >> 23);
+    if (bits == 0 || ex >= 255) {
+        s = inv = 1.0f;
+        return;
+    }
+    const int e = max(ex - 127, -100);
+    s = __int_as_float((127 + 14 - e) << 23);
+    inv = __int_as_float((127 + e - 14) << 23);
+}
+
+__global__ void __launch_bounds__(256) vconv_kernel(const __nv_bfloat16* v, __half* v16, const uint32_t* vmax,
+                                                    float* vinv, uint32_t k_pad, uint32_t n_rows,
+                                                    const uint8_t* valid)
+{
+    const uint32_t kvh = blockIdx.y;
+    float s, inv;
+    v_scale(vmax[kvh], s, inv);
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+        vinv[kvh] = inv;
+    const uint4* src = reinterpret_cast<const uint4*>(v + uint64_t(kvh) * k_pad * TD);
+    uint4* dst = reinterpret_cast<uint4*>(v16 + uint64_t(kvh) * k_pad * TD);
+    const uint64_t chunks = uint64_t(k_pad) * (TD / 8);
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < chunks; i += uint64_t(gridDim.x) * blockDim.x) {
+        const uint32_t row = uint32_t(i / (TD / 8));
+        uint4 out = make_uint4(0, 0, 0, 0);
+        if (row < n_rows && (!valid || valid[row])) {
+            const uint4 w = src[i];
+            const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float a = __uint_as_float(in[k] << 16) * s, b = __uint_as_float(in[k] & 0xFFFF0000u) * s;
+                o[k] = pack_half2(a, b);
+            }
+            out = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        dst[i] = out;
+    }
+}
+
+// ---- host ----------------------------------------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// [heads][rows][128] 16-bit tiles, boxes of 128 rows x 64 values, 128-byte swizzle, zero fill past `rows`.
+bool head_map(CUtensorMap* map, const void* ptr, bool bf16, uint32_t rows, uint32_t heads)
+{
+    auto enc = encode_fn();
+    if (!enc)
+        return false;
+    cuuint64_t dims[3] = {TD, rows, heads};
+    cuuint64_t strides[2] = {uint64_t(TD) * 2, uint64_t(rows) * TD * 2};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+} // namespace
+
+cudaError_t launch_v_to_f16(const void* v, void* v16, uint32_t* vmax, float* vinv, uint32_t kv_heads, uint32_t k_pad,
+                            uint32_t n_rows, const uint8_t* valid, int num_sms, cudaStream_t st)
+{
+    cudaError_t e = cudaMemsetAsync(vmax, 0, kv_heads * sizeof(uint32_t), st);
+    if (e != cudaSuccess)
+        return e;
+    const uint64_t chunks = uint64_t(k_pad) * (TD / 8);
+    uint32_t bx = uint32_t((chunks + 255) / 256);
+    const uint32_t cap = uint32_t((num_sms * 8 + kv_heads - 1) / kv_heads);
+    bx = bx < 1 ? 1 : (bx > cap ? cap : bx);
+    vmax_kernel<<<dim3(bx, kv_heads), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(v), vmax, k_pad, n_rows, valid);
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return e;
+    vconv_kernel<<<dim3(bx, kv_heads), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(v), static_cast<__half*>(v16),
+                                                      vmax, vinv, k_pad, n_rows, valid);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attn_tc(const AttnParams& a, int dtype, const void* v16, const float* vinv, int* err,
+                           cudaStream_t st)
+{
+    if (a.n_q == 0 || a.heads == 0)
+        return cudaSuccess;
+    TcParams p;
+    const bool bf = dtype == kBF16;
+    if (!head_map(&p.tq, a.q, bf, a.q_pad, a.heads) || !head_map(&p.tk, a.k, bf, a.k_pad, a.kv_heads) ||
+        !head_map(&p.tv, bf ? v16 : a.v, false, a.k_pad, a.kv_heads))
+        return cudaErrorInvalidValue;
+    p.o = a.o;
+    p.err = err;
+    p.vinv = bf ? vinv : nullptr;
+    p.qk_fmt = bf ? 1u : 0u;
+    p.n_q = a.n_q;
+    p.q_pad = a.q_pad;
+    p.n_k = a.n_k;
+    p.k_pad = a.k_pad;
+    p.heads = a.heads;
+    p.kv_heads = a.kv_heads;
+    p.q_pos0 = a.q_pos0;
+    p.block = a.block;
+    p.width = a.width;
+    p.n_tiles = (a.q_pad + 2 * TBM - 1) / (2 * TBM);
+    p.scale_log2 = a.scale * kLog2e;
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL);
+    if (e != cudaSuccess)
+        return e;
+    attn_tc_kernel<<<dim3(p.n_tiles, a.heads), TNT, SMEM_TOTAL, st>>>(p);
+    return cudaGetLastError();
+}
+
+} // namespace mako

@@ -16,6 +16,8 @@
 struct mako_attn_ctx {
     int device = 0;
     int num_sms = 148;
+    int cc_major = 0;
+    int* err = nullptr;      // device flag the pipelined kernels set when a wait times out
     int prefill_kernel = 0;  // MAKO_OPT_PREFILL_KERNEL
     int decode_route = 1;    // MAKO_OPT_DECODE_ROUTE
     uint64_t launches = 0;   // kernels enqueued
@@ -133,6 +135,17 @@ int mako_attn_create(int device, mako_attn_ctx** out)
         return fail(MAKO_ENOMEM, "context");
     ctx->device = device;
     ctx->num_sms = prop.multiProcessorCount;
+    ctx->cc_major = prop.major;
+    {
+        DeviceGuard dg(device);
+        if ((e = cudaMalloc(&ctx->err, sizeof(int))) != cudaSuccess ||
+            (e = cudaMemset(ctx->err, 0, sizeof(int))) != cudaSuccess) {
+            if (ctx->err)
+                cudaFree(ctx->err);
+            delete ctx;
+            return cuda_fail("context error flag", e);
+        }
+    }
     *out = ctx;
     g_error.clear();
     return MAKO_OK;
@@ -145,6 +158,8 @@ int mako_attn_destroy(mako_attn_ctx* ctx)
     int rc = MAKO_OK;
     {
         DeviceGuard dg(ctx->device);
+        if (ctx->err)
+            cudaFree(ctx->err);
         for (auto& kv : ctx->scratch)
             if (kv.second.ptr) {
                 cudaError_t e = cudaFree(kv.second.ptr);
@@ -179,6 +194,21 @@ int mako_attn_launches(mako_attn_ctx* ctx, uint64_t* out)
     if (!ctx || !out)
         return fail(MAKO_EINVAL, "null argument");
     *out = ctx->launches;
+    return MAKO_OK;
+}
+
+int mako_attn_device_error(mako_attn_ctx* ctx, int* out)
+{
+    if (!ctx || !out)
+        return fail(MAKO_EINVAL, "null argument");
+    DeviceGuard dg(ctx->device);
+    int v = 0;
+    cudaError_t e = cudaMemcpy(&v, ctx->err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess)
+        return cuda_fail("read device error flag", e);
+    if (v && (e = cudaMemset(ctx->err, 0, sizeof(int))) != cudaSuccess)
+        return cuda_fail("reset device error flag", e);
+    *out = v;
     return MAKO_OK;
 }
 
@@ -252,8 +282,29 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
     p.block = block;
     p.width = width;
     p.scale = 1.0f / sqrtf(float(dim));
-    if (ctx->prefill_kernel == 2)
-        return fail(MAKO_ENOTSUP, "attention: the tcgen05 kernel is not in this build");
+    const bool tc_ok = dim == 128 && ctx->cc_major == 10;
+    if (ctx->prefill_kernel == 2 && !tc_ok)
+        return fail(MAKO_ENOTSUP, "attention: the tcgen05 kernel takes 128-wide heads on sm_100 (got %u, sm_%d)", dim,
+                    ctx->cc_major * 10);
+    if (tc_ok && ctx->prefill_kernel != 1) {
+        void *v16 = nullptr, *vmax = nullptr, *vinv = nullptr;
+        if (dtype == MAKO_BF16) {
+            if (int rc = scratch(ctx, "v16", size_t(kv_heads) * k_pad * dim * 2, &v16))
+                return rc;
+            if (int rc = scratch(ctx, "vmax", size_t(kv_heads) * 4, &vmax))
+                return rc;
+            if (int rc = scratch(ctx, "vinv", size_t(kv_heads) * 4, &vinv))
+                return rc;
+            cudaError_t e = mako::launch_v_to_f16(v, v16, static_cast<uint32_t*>(vmax), static_cast<float*>(vinv),
+                                                  kv_heads, k_pad, n_k, nullptr, ctx->num_sms, st);
+            if (e != cudaSuccess)
+                return cuda_fail("attention (V to fp16)", e);
+            ctx->launches += 2;
+        }
+        ctx->launches += 1;
+        return launched("attention (tcgen05)",
+                        mako::launch_attn_tc(p, dtype, v16, static_cast<const float*>(vinv), ctx->err, st));
+    }
     ctx->launches += 1;
     return launched("attention", mako::launch_attn_mma(p, dtype, dim, false, false, st));
 }

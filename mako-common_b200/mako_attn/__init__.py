@@ -19,7 +19,7 @@ UINT32_MAX = 0xFFFFFFFF
 # Every symbol include/mako_attn.h declares, for the load check.
 SYMBOLS = (
     "mako_attn_last_error", "mako_attn_version", "mako_attn_create", "mako_attn_destroy", "mako_attn_set_option",
-    "mako_attn_launches", "mako_attention", "mako_attention_decode", "mako_cube_select", "mako_attention_sparse",
+    "mako_attn_launches", "mako_attn_device_error", "mako_attention", "mako_attention_decode", "mako_cube_select", "mako_attention_sparse",
     "mako_attention_block_sparse",
 )
 
@@ -48,6 +48,7 @@ def lib():
     L.mako_attn_destroy.argtypes = [p]
     L.mako_attn_set_option.argtypes = [p, i32, i64]
     L.mako_attn_launches.argtypes = [p, ctypes.POINTER(ctypes.c_uint64)]
+    L.mako_attn_device_error.argtypes = [p, ctypes.POINTER(ctypes.c_int)]
     L.mako_attention.argtypes = [p, p, i32, p, p, p, p] + [u32] * 10
     L.mako_attention_decode.argtypes = [p, p, i32, p, p, p, p, u32, p, u32, u32, u32, u32, u32]
     L.mako_cube_select.argtypes = ([p, p, i32, p, p] + [u32] * 4 + [p, u32, ctypes.POINTER(p), ctypes.POINTER(p)]
@@ -120,6 +121,12 @@ class Context:
 
     def set_option(self, option: int, value: int):
         _check(lib().mako_attn_set_option(self._h, option, value))
+
+    def device_error(self) -> int:
+        """Reads and clears the device error flag (0: every pipelined wait completed)."""
+        n = ctypes.c_int()
+        _check(lib().mako_attn_device_error(self._h, ctypes.byref(n)))
+        return n.value
 
     def launches(self) -> int:
         n = ctypes.c_uint64()

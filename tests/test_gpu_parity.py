@@ -62,10 +62,14 @@ DENSE = [
 
 
 @pytest.mark.parametrize("name,kw", DENSE, ids=[n for n, _ in DENSE])
-@pytest.mark.parametrize("kernel", [0, 1])
+@pytest.mark.parametrize("kernel", [0, 1, 2], ids=["auto", "mma", "tcgen05"])
 def test_dense(ctx, oracle, name, kw, kernel):
+    """kernel 0: the default choice (tcgen05 for 128-wide heads), 1: the portable mma.sync kernel, 2: tcgen05."""
+    if kernel == 2 and kw["dim"] != 128:
+        pytest.skip("the tcgen05 kernel takes 128-wide heads")
     case = C.dense_case(**kw)
     got = run_dense(ctx, case, kernel)
+    assert ctx.device_error() == 0
     want = oracle_dense(oracle, case)
     ok, stats = C.within(got[:case["n_q"]], want)
     assert ok, f"{name}: max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
@@ -218,6 +222,19 @@ def test_block_sparse_lists(ctx, oracle):
     ok, stats = C.within(got, want)
     assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
     assert np.all(got[3 * 64:4 * 64, 128:256] == 0.0)
+
+
+def test_tcgen05_rejects_other_widths(ctx):
+    import torch
+    import mako_attn
+    q = torch.zeros(64 * 64, dtype=torch.float16, device="cuda")
+    o = torch.zeros(64 * 64, dtype=torch.float32, device="cuda")
+    ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 2)
+    try:
+        with pytest.raises(mako_attn.MakoError, match="tcgen05"):
+            ctx.attention(q, q, q, o, 10, 64, 10, 64, 1, 1, 0, 0, 64)
+    finally:
+        ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 0)
 
 
 def test_argument_errors(ctx):
