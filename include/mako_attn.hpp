@@ -1,0 +1,87 @@
+// mako_attn.hpp -- C++ shim over the C ABI (mako_attn.h) with the method names, argument order and error behaviour
+// of mako-common's TransformerRuntime attention members (src/models/runtime.hpp:90-111): device pointers and a
+// cudaStream_t take the place of MTL::Buffer* and the command encoder, and a failed call throws std::runtime_error
+// with the library's message, as the reference throws before encoding (src/models/runtime.cpp:266-267,290-291,
+// 311-312).  Calls are stream-ordered and do not synchronise; one Attention object per thread / stream.
+#pragma once
+
+#include "mako_attn.h"
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace mako::attn {
+
+enum class Dtype : int { f16 = MAKO_F16, bf16 = MAKO_BF16 };
+
+class Attention {
+public:
+    static constexpr uint32_t kHeadDim = 128;  // src/models/runtime.hpp:33
+
+    explicit Attention(int device = 0, Dtype dtype = Dtype::f16) : dtype_(int(dtype))
+    {
+        check(mako_attn_create(device, &ctx_));
+    }
+    ~Attention() { mako_attn_destroy(ctx_); }
+    Attention(const Attention&) = delete;
+    Attention& operator=(const Attention&) = delete;
+
+    void set_dtype(Dtype d) { dtype_ = int(d); }
+    void set_stream(void* stream) { stream_ = stream; }
+
+    // TransformerRuntime::attention (src/models/runtime.hpp:90-95).
+    void attention(const void* q, const void* k, const void* v, float* o, uint32_t n_q, uint32_t q_pad, uint32_t n_k,
+                   uint32_t k_pad, uint32_t heads, uint32_t kv_heads, uint32_t q_pos0, uint32_t block,
+                   uint32_t dim = kHeadDim)
+    {
+        check(mako_attention(ctx_, stream_, dtype_, q, k, v, o, n_q, q_pad, n_k, k_pad, heads, kv_heads, q_pos0, block,
+                             dim, 0));
+    }
+    // TransformerRuntime::cube_select (src/models/runtime.hpp:104-106): sel / nsel become this object's scratch.
+    void cube_select(const void* q, const void* k, uint32_t heads, uint32_t q_pad, uint32_t k_pad, uint32_t n_cubes,
+                     const uint32_t* cnt, uint32_t topk, uint16_t*& sel, uint16_t*& nsel, uint32_t local = 0,
+                     uint32_t stride = 0)
+    {
+        check(mako_cube_select(ctx_, stream_, dtype_, q, k, heads, q_pad, k_pad, n_cubes, cnt, topk, &sel, &nsel, local,
+                               stride));
+    }
+    // TransformerRuntime::attention_sparse (src/models/runtime.hpp:107-110).
+    void attention_sparse(const void* q, const void* k, const void* v, float* o, uint32_t n_q, uint32_t q_pad,
+                          uint32_t n_k, uint32_t k_pad, uint32_t heads, uint32_t kv_heads, uint32_t width,
+                          uint32_t n_cubes, uint32_t topk, uint32_t dense0, uint32_t dense1, const uint16_t* sel,
+                          const uint16_t* nsel, const uint8_t* valid, const int32_t* map)
+    {
+        check(mako_attention_sparse(ctx_, stream_, dtype_, q, k, v, o, n_q, q_pad, n_k, k_pad, heads, kv_heads, width,
+                                    n_cubes, topk, dense0, dense1, sel, nsel, valid, map));
+    }
+    // Batched decode over a KV cache (no reference member: its decode step is attention() with n_q = 1).
+    void attention_decode(const void* q, const void* k, const void* v, float* o, uint32_t batch, const int32_t* kv_len,
+                          uint32_t max_kv_len, uint32_t heads, uint32_t kv_heads, uint32_t dim, uint32_t k_stride)
+    {
+        check(mako_attention_decode(ctx_, stream_, dtype_, q, k, v, o, batch, kv_len, max_kv_len, heads, kv_heads, dim,
+                                    k_stride));
+    }
+    // The check gpu::Runtime::finish makes after a command buffer (src/gpu/runtime.cpp:466-471): throws if a
+    // pipelined kernel gave up on a wait.  Synchronises the device.
+    void finish()
+    {
+        int err = 0;
+        check(mako_attn_device_error(ctx_, &err));
+        if (err)
+            throw std::runtime_error("attention: a kernel gave up on a pipeline wait (code " + std::to_string(err) + ")");
+    }
+    mako_attn_ctx* handle() const { return ctx_; }
+
+private:
+    static void check(int rc)
+    {
+        if (rc != MAKO_OK)
+            throw std::runtime_error(mako_attn_last_error());
+    }
+    mako_attn_ctx* ctx_ = nullptr;
+    void* stream_ = nullptr;
+    int dtype_ = MAKO_F16;
+};
+
+} // namespace mako::attn

@@ -1,0 +1,26 @@
+// Host-side check of the C++ shim (include/mako_attn.hpp): it compiles against the C ABI, links libmako_attn.so and
+// turns the library's statuses into std::runtime_error like TransformerRuntime does.  Needs no GPU: without a device
+// the constructor must throw; with one, an argument the reference rejects (a head width of 96,
+// src/models/runtime.cpp:266-267) must throw before anything is enqueued.
+#include "mako_attn.hpp"
+
+#include <cstdio>
+#include <cstring>
+
+int main()
+{
+    try {
+        mako::attn::Attention attn(0);
+        try {
+            attn.attention(nullptr, nullptr, nullptr, nullptr, 1, 64, 1, 128, 1, 1, 0, 0, 96);
+        } catch (const std::runtime_error& e) {
+            std::printf("rejected: %s\n", e.what());
+            return std::strstr(e.what(), "heads of 96") ? 0 : 1;
+        }
+        std::printf("a head width of 96 was accepted\n");
+        return 1;
+    } catch (const std::runtime_error& e) {
+        std::printf("no device: %s\n", e.what());
+        return std::strlen(e.what()) ? 0 : 1;
+    }
+}

@@ -54,3 +54,15 @@ def test_create_without_a_device_reports_the_cuda_error():
     rc = L.mako_attn_create(0, ctypes.byref(h))
     assert rc in (mako_attn.ECUDA, mako_attn.EINVAL) and not h.value
     assert L.mako_attn_last_error()
+
+
+def test_cpp_shim_compiles_links_and_throws(tmp_path):
+    """include/mako_attn.hpp over libmako_attn.so: a bad call (or no device) surfaces as std::runtime_error."""
+    import subprocess
+    lib_dir = os.path.join(ROOT, "mako-common_b200", "mako_attn")
+    exe = str(tmp_path / "shim_check")
+    subprocess.run(["/usr/bin/g++", "-std=c++17", "-O1", "-I", os.path.join(ROOT, "include"),
+                    os.path.join(ROOT, "tests", "shim_check.cpp"), "-L", lib_dir, "-lmako_attn",
+                    f"-Wl,-rpath,{lib_dir}", "-o", exe], check=True)
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
