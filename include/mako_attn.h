@@ -84,6 +84,20 @@ int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const voi
                           float* o, uint32_t batch, const int32_t* kv_len, uint32_t max_kv_len, uint32_t heads,
                           uint32_t kv_heads, uint32_t dim, uint32_t k_stride);
 
+/* mako_attention_decode without any device allocation and without a context, for callers that cannot call
+ * cudaMalloc: a process whose device memory is wholly committed elsewhere (a fixed pool it reserved up front, or
+ * memory it borrowed under a lending protocol and must not grow beyond), or a loop that cannot afford
+ * cudaMalloc / cudaFree synchronising the device.  No counterpart in the reference.
+ * Same arguments and results as mako_attention_decode, on the current device.  The split partials live in one
+ * file-scope device array of 4 MiB that every GPU loading this library holds until the process exits; the call
+ * picks larger splits when needed so that they fit, and returns MAKO_EINVAL when even one split per sequence would
+ * not (batch * heads * (4 * dim + 8) bytes above 4 MiB).  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream capture.  Every call uses the same array,
+ * so calls that overlap on the GPU (other streams, other threads) race: serialise them. */
+int mako_attention_decode_noalloc(void* stream, int dtype, const void* q, const void* k, const void* v, float* o,
+                                  uint32_t batch, const int32_t* kv_len, uint32_t max_kv_len, uint32_t heads,
+                                  uint32_t kv_heads, uint32_t dim, uint32_t k_stride);
+
 /* Cube selection for block-sparse attention over 128-wide heads: per head and query cube (64 rows), the `topk`
  * key cubes whose mean-pooled k scores highest against the cube's mean-pooled q (cnt[c]: valid rows of cube c,
  * device uint32 [n_cubes]; invalid rows must be zero).  local 0: by score; 1: the query cube itself first; 3: also

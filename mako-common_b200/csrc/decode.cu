@@ -11,7 +11,9 @@
 // Kernel 2 (decode_combine_kernel): the log-sum-exp merge of a row's splits into o.
 #include "common.cuh"
 #include "kernels.h"
+#include "mako_attn.h"
 
+#include <mutex>
 #include <type_traits>
 
 namespace mako {
@@ -272,3 +274,110 @@ cudaError_t launch_decode(const DecodeParams& p, int dtype, int dim, cudaStream_
 }
 
 } // namespace mako
+
+// ---- decode without device allocation ------------------------------------------------------------------------------
+//
+// Some callers cannot call cudaMalloc: a process whose device memory is entirely committed to another owner (a fixed
+// pre-reserved pool, or memory borrowed under a lending protocol such as mako's lender / borrower, which must not
+// grow outside its loan), or a latency-critical loop that cannot accept cudaMalloc / cudaFree synchronising the
+// device.  mako_attention_decode_noalloc serves them: the split-KV partials live in the static device array below
+// instead of context scratch, so a call allocates nothing and needs no context.
+
+namespace {
+
+// The partials of one call: o [batch][heads][n_splits][dim] fp32, then (max, sum) [batch][heads][n_splits].  Every
+// GPU that loads this library holds this array until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// The array's device address on `device` (current), looked up once per device.  In host code the array's name is
+// only a host-side stand-in, never a usable device address.
+int scratch_address(int device, void** out)
+{
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+        if (e != cudaSuccess || !p)
+            return mako::set_error(MAKO_ECUDA, "decode_noalloc: address of the static scratch on device %d: %s", device,
+                                   cudaGetErrorString(e));
+        g_scratch_addr[device] = p;
+    }
+    *out = g_scratch_addr[device];
+    return MAKO_OK;
+}
+
+} // namespace
+
+extern "C" int mako_attention_decode_noalloc(void* stream, int dtype, const void* q, const void* k, const void* v,
+                                             float* o, uint32_t batch, const int32_t* kv_len, uint32_t max_kv_len,
+                                             uint32_t heads, uint32_t kv_heads, uint32_t dim, uint32_t k_stride)
+{
+    using mako::set_error;
+    if (dtype != MAKO_F16 && dtype != MAKO_BF16)
+        return set_error(MAKO_EINVAL, "decode_noalloc: element type %d", dtype);
+    if (dim != 64 && dim != 128 && dim != 256)
+        return set_error(MAKO_EINVAL, "decode_noalloc: heads of %u", dim);
+    if (!heads || !kv_heads || heads % kv_heads)
+        return set_error(MAKO_EINVAL, "decode_noalloc: %u heads over %u kv heads", heads, kv_heads);
+    if (max_kv_len > k_stride)
+        return set_error(MAKO_EINVAL, "decode_noalloc: max_kv_len %u beyond the cache's %u rows", max_kv_len, k_stride);
+    auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!q || !k || !v || !o || !kv_len || !aligned(q) || !aligned(k) || !aligned(v) || !aligned(o))
+        return set_error(MAKO_EINVAL, "decode_noalloc: null or unaligned tensor (16-byte alignment)");
+    if (batch == 0)
+        return MAKO_OK;
+    int device = 0, sms = 148;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess || device < 0 || device >= kMaxDevices)
+        return set_error(MAKO_ECUDA, "decode_noalloc: current device: %s", cudaGetErrorString(e));
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+        return set_error(MAKO_ECUDA, "decode_noalloc: SM count: %s", cudaGetErrorString(e));
+
+    // The split plan of mako_attention_decode, with larger chunks when its partials would not fit the array.
+    uint32_t chunk, n_splits;
+    mako::decode_plan(max_kv_len, batch, kv_heads, heads, sms, &chunk, &n_splits);
+    const uint64_t per_split = uint64_t(batch) * heads * (uint64_t(dim) * 4 + 8);
+    if (per_split > kNoAllocScratchBytes)
+        return set_error(MAKO_EINVAL,
+                         "decode_noalloc: %u sequences x %u heads of %u need %llu bytes of partials, beyond the %zu-byte "
+                         "static scratch (use mako_attention_decode)",
+                         batch, heads, dim, (unsigned long long)per_split, kNoAllocScratchBytes);
+    while (uint64_t(n_splits) * per_split > kNoAllocScratchBytes) {
+        chunk += 64;
+        n_splits = max_kv_len ? (max_kv_len + chunk - 1) / chunk : 1u;
+    }
+    void* base = nullptr;
+    if (int rc = scratch_address(device, &base))
+        return rc;
+
+    mako::DecodeParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = o;
+    p.kv_len = kv_len;
+    p.len = 0;
+    p.q_bstride = uint64_t(heads) * dim;
+    p.q_hstride = dim;
+    p.k_hstride = uint64_t(k_stride) * dim;
+    p.k_bstride = uint64_t(kv_heads) * p.k_hstride;
+    p.o_bstride = uint64_t(heads) * dim;
+    p.batch = batch;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.chunk = chunk;
+    p.n_splits = n_splits;
+    p.scale = 1.0f / sqrtf(float(dim));
+    const size_t o_bytes = (size_t(batch) * heads * n_splits * dim * 4 + 255) / 256 * 256;
+    p.o_part = static_cast<float*>(base);
+    p.ml_part = reinterpret_cast<float2*>(static_cast<unsigned char*>(base) + o_bytes);
+    if ((e = mako::launch_decode(p, dtype, int(dim), static_cast<cudaStream_t>(stream))) != cudaSuccess)
+        return set_error(MAKO_ECUDA, "decode_noalloc: %s (%s)", cudaGetErrorString(e), cudaGetErrorName(e));
+    mako::clear_error();
+    return MAKO_OK;
+}

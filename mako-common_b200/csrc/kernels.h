@@ -8,6 +8,10 @@ namespace mako {
 
 enum Dtype : int { kF16 = 0, kBF16 = 1 };
 
+// This thread's message for mako_attn_last_error(): set_error formats it and returns `code`.
+int set_error(int code, const char* fmt, ...);
+void clear_error();
+
 // One attention launch: the fields of the reference's AttnArgs (src/kernels/ops.metal:54-64) plus, for the
 // block-sparse form, those of SparseAttnArgs (ops.metal:1029-1034) and its index buffers.
 struct AttnParams {

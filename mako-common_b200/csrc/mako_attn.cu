@@ -29,10 +29,11 @@ struct mako_attn_ctx {
 };
 
 namespace {
-
 thread_local std::string g_error;
+} // namespace
 
-int fail(int code, const char* fmt, ...)
+namespace mako {
+int set_error(int code, const char* fmt, ...)
 {
     char buf[512];
     va_list ap;
@@ -41,6 +42,16 @@ int fail(int code, const char* fmt, ...)
     va_end(ap);
     g_error = buf;
     return code;
+}
+void clear_error() { g_error.clear(); }
+} // namespace mako
+
+namespace {
+
+template <typename... A>
+int fail(int code, const char* fmt, A... args)
+{
+    return mako::set_error(code, fmt, args...);
 }
 
 int cuda_fail(const char* what, cudaError_t e)

@@ -20,7 +20,7 @@ UINT32_MAX = 0xFFFFFFFF
 SYMBOLS = (
     "mako_attn_last_error", "mako_attn_version", "mako_attn_create", "mako_attn_destroy", "mako_attn_set_option",
     "mako_attn_launches", "mako_attn_device_error", "mako_attention", "mako_attention_decode", "mako_cube_select", "mako_attention_sparse",
-    "mako_attention_block_sparse",
+    "mako_attention_block_sparse", "mako_attention_decode_noalloc",
 )
 
 _lib = None
@@ -55,6 +55,7 @@ def lib():
                                    + [u32, u32])
     L.mako_attention_sparse.argtypes = [p, p, i32, p, p, p, p] + [u32] * 11 + [p, p, p, p]
     L.mako_attention_block_sparse.argtypes = [p, p, i32, p, p, p, p, u32, u32, u32, p, p, u32]
+    L.mako_attention_decode_noalloc.argtypes = [p, i32, p, p, p, p, u32, p, u32, u32, u32, u32, u32]
     for name in SYMBOLS:
         if name != "mako_attn_last_error":
             getattr(L, name).restype = i32
@@ -84,6 +85,14 @@ def dtype_code(t) -> int:
     if t.dtype == torch.bfloat16:
         return BF16
     raise TypeError(f"16-bit float tensors only, got {t.dtype}")
+
+
+def attention_decode_noalloc(q, k, v, o, kv_len, max_kv_len, heads, kv_heads, dim, k_stride, stream=None):
+    """mako_attention_decode_noalloc: the decode with its partials in the library's static device array -- no
+    context, no device allocation (for callers that cannot allocate; calls must not overlap on the GPU)."""
+    _check(lib().mako_attention_decode_noalloc(_stream(stream), dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                               kv_len.numel(), _ptr(kv_len), max_kv_len, heads, kv_heads, dim,
+                                               k_stride))
 
 
 class _DeviceArray:
