@@ -155,7 +155,6 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
         if (lane == 0 && nb > 0) {
             const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, TBM, TBN);
             const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, TBM, TD);
-            bool ok = mbar_wait(q_full, 0, WAIT_LIMIT);
             auto qk = [&](uint32_t x, uint32_t stage) {
 #pragma unroll
                 for (uint32_t ks = 0; ks < TD / 16; ++ks) {
@@ -170,7 +169,8 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                     umma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
                             sdesc(sV + stage * TILE_BYTES + kk * 2048, BOX_BYTES, 1024), idesc_pv, acc || kk > 0);
             };
-            if (ok && (ok = mbar_wait(k_full(0), 0, WAIT_LIMIT))) {
+            bool ok = mbar_wait(q_full, 0, WAIT_LIMIT) && mbar_wait(k_full(0), 0, WAIT_LIMIT);
+            if (ok) {
                 fence_after();
                 qk(0, 0);
                 umma_commit(s_full(0));
@@ -178,38 +178,49 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                 umma_commit(s_full(1));
                 umma_commit(k_empty(0));
             }
-            for (uint32_t j = 0; j < nb && ok; ++j) {
-                const uint32_t s = j % TNS, ph = (j / TNS) & 1;
-                const bool nxt = j + 1 < nb;
-                const uint32_t s1 = (j + 1) % TNS, ph1 = ((j + 1) / TNS) & 1;
-                // tile A
-                if (!(ok = mbar_wait(p_full(0), j & 1, WAIT_LIMIT) && mbar_wait(v_full(s), ph, WAIT_LIMIT)))
-                    break;
-                fence_after();
-                pv(0, s, j > 0);
-                umma_commit(pv_done(0));
-                if (nxt) {
-                    if (!(ok = mbar_wait(k_full(s1), ph1, WAIT_LIMIT) && mbar_wait(pv_done(0), j & 1, WAIT_LIMIT)))
-                        break;
-                    fence_after();
-                    qk(0, s1);
-                    umma_commit(s_full(0));
+            // Per tile X the next P.V and the next Q.K^T: PV_X(j) needs P_X(j) from the softmax and V_j; QK_X(j+1)
+            // needs K_{j+1} and PV_X(j) finished (it overwrites the P that PV_X(j) reads).  Whichever product is
+            // ready is issued, so one tile's wait is filled with the other tile's work.
+            uint32_t pv_next[2] = {0, 0}, qk_next[2] = {1, 1};
+            uint32_t k_ok = 1, v_ok = 0;  // K / V tiles seen landed: [0, k_ok), [0, v_ok)
+            long long idle_since = clock64();
+            while (ok && (pv_next[0] < nb || pv_next[1] < nb)) {
+                bool progressed = false;
+#pragma unroll
+                for (uint32_t x = 0; x < 2; ++x) {
+                    const uint32_t j = pv_next[x];
+                    if (j < nb && qk_next[x] > j) {
+                        if (v_ok == j && mbar_try_wait(v_full(j % TNS), (j / TNS) & 1))
+                            v_ok = j + 1;
+                        if (v_ok > j && mbar_try_wait(p_full(x), j & 1)) {
+                            fence_after();
+                            pv(x, j % TNS, j > 0);
+                            umma_commit(pv_done(x));
+                            pv_next[x] = j + 1;
+                            if (pv_next[x ^ 1] > j)  // both tiles' PV of V_j issued: the stage frees when they finish
+                                umma_commit(v_empty(j % TNS));
+                            progressed = true;
+                        }
+                    }
+                    const uint32_t j1 = qk_next[x];
+                    if (j1 < nb && pv_next[x] == j1) {
+                        if (k_ok == j1 && mbar_try_wait(k_full(j1 % TNS), (j1 / TNS) & 1))
+                            k_ok = j1 + 1;
+                        if (k_ok > j1 && mbar_try_wait(pv_done(x), (j1 - 1) & 1)) {
+                            fence_after();
+                            qk(x, j1 % TNS);
+                            umma_commit(s_full(x));
+                            qk_next[x] = j1 + 1;
+                            if (qk_next[x ^ 1] > j1)
+                                umma_commit(k_empty(j1 % TNS));
+                            progressed = true;
+                        }
+                    }
                 }
-                // tile B
-                if (!(ok = mbar_wait(p_full(1), j & 1, WAIT_LIMIT)))
-                    break;
-                fence_after();
-                pv(1, s, j > 0);
-                umma_commit(pv_done(1));
-                umma_commit(v_empty(s));
-                if (nxt) {
-                    if (!(ok = mbar_wait(pv_done(1), j & 1, WAIT_LIMIT)))
-                        break;
-                    fence_after();
-                    qk(1, s1);
-                    umma_commit(s_full(1));
-                    umma_commit(k_empty(s1));
-                }
+                if (progressed)
+                    idle_since = clock64();
+                else if (clock64() - idle_since > WAIT_LIMIT)
+                    ok = false;
             }
             if (!ok)
                 atomicExch(p.err, 2);
@@ -242,16 +253,21 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             for (int c = 0; c < 4; ++c)
                 reg_fence(r[c]);
             const uint32_t j0 = j * TBN;
-            const bool plain = j0 + TBN <= lim1;
-            float mx = -INFINITY;
+            if (j0 + TBN > lim1) {  // a tile the mask cuts: keys at or past this row's limit drop out
 #pragma unroll
-            for (int c = 0; c < TBN; ++c) {
-                float v = __uint_as_float(r[c >> 5][c & 31]) * scale;
-                if (!plain && j0 + c >= lim)
-                    v = -INFINITY;
-                r[c >> 5][c & 31] = __float_as_uint(v);
-                mx = fmaxf(mx, v);
+                for (int c = 0; c < TBN; ++c)
+                    if (j0 + c >= lim)
+                        r[c >> 5][c & 31] = 0xFF800000u;  // -inf
             }
+            // Row maximum of the raw scores (scale > 0 keeps the order), three at a time, four chains.
+            float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int c = 0; c < TBN; c += 8)
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    mq[t] = max3f(mq[t], __uint_as_float(r[(c + 2 * t) >> 5][(c + 2 * t) & 31]),
+                                  __uint_as_float(r[(c + 2 * t + 1) >> 5][(c + 2 * t + 1) & 31]));
+            const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
             float f = 1.0f;
             bool resc = false;
             if (mx > m + 8.0f) {
@@ -260,16 +276,28 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                 l *= f;
                 resc = true;
             }
+            // P = 2^(s * scale - m), two lanes per FMA; a row with no visible key so far has every s = -inf.
+            const float mneg = m == -INFINITY ? 0.0f : -m;
+            const uint64_t scale2 = pack2(scale, scale), mneg2 = pack2(mneg, mneg);
             uint32_t pk[2][32];
-            float sum = 0.0f;
+            uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
 #pragma unroll
             for (int c = 0; c < TBN / 2; ++c) {
-                const float a = m == -INFINITY ? 0.0f : ex2(__uint_as_float(r[(2 * c) >> 5][(2 * c) & 31]) - m);
-                const float b = m == -INFINITY ? 0.0f : ex2(__uint_as_float(r[(2 * c + 1) >> 5][(2 * c + 1) & 31]) - m);
-                sum += a + b;
+                const uint64_t x = pack2(__uint_as_float(r[(2 * c) >> 5][(2 * c) & 31]),
+                                         __uint_as_float(r[(2 * c + 1) >> 5][(2 * c + 1) & 31]));
+                float a, b;
+                unpack2(ffma2(x, scale2, mneg2), a, b);
+                a = ex2(a);
+                b = ex2(b);
+                sum2[c & 1] = fadd2(sum2[c & 1], pack2(a, b));
                 pk[c >> 5][c & 31] = pack_half2(a, b);
             }
-            l += sum;
+            {
+                float s0, s1, s2, s3;
+                unpack2(sum2[0], s0, s1);
+                unpack2(sum2[1], s2, s3);
+                l += (s0 + s1) + (s2 + s3);
+            }
             tmem_st32(tl + colS, pk[0]);
             tmem_st32(tl + colS + 32, pk[1]);
             // Rescale this tile's O before P.V adds to it (PV_X(j-1) finished before QK_X(j) was issued).

@@ -149,6 +149,38 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[32])
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
+// ---- packed fp32 arithmetic (sm_100) --------------------------------------------------------------------------------
+
+__device__ __forceinline__ float max3f(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t pack2(float lo, float hi)
+{
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};\n" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi)
+{
+    asm("mov.b64 {%0, %1}, %2;\n" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// (a * b + c) on two fp32 lanes at once.
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // ---- descriptors ---------------------------------------------------------------------------------------------------
 
 // Shared-memory matrix descriptor (sm_100 UMMA): start address, leading / stride byte offsets, version 1, 128-byte
