@@ -425,9 +425,32 @@ int sparse_common(mako_attn_ctx* ctx, void* stream, int dtype, mako::AttnParams&
     if (dg.err != cudaSuccess)
         return cuda_fail("set device", dg.err);
     p.scale = 1.0f / sqrtf(128.0f);
+    auto st = static_cast<cudaStream_t>(stream);
+    const bool tc_ok = ctx->cc_major == 10;
+    if (ctx->prefill_kernel == 2 && !tc_ok)
+        return fail(MAKO_ENOTSUP, "attention_sparse: the tcgen05 kernel needs sm_100 (sm_%d)", ctx->cc_major * 10);
+    if (tc_ok && ctx->prefill_kernel != 1) {
+        void *v16 = nullptr, *vmax = nullptr, *vinv = nullptr;
+        if (dtype == MAKO_BF16) {
+            if (int rc = scratch(ctx, "v16", size_t(p.kv_heads) * p.k_pad * 128 * 2, &v16))
+                return rc;
+            if (int rc = scratch(ctx, "vmax", size_t(p.kv_heads) * 4, &vmax))
+                return rc;
+            if (int rc = scratch(ctx, "vinv", size_t(p.kv_heads) * 4, &vinv))
+                return rc;
+            cudaError_t e = mako::launch_v_to_f16(p.v, v16, static_cast<uint32_t*>(vmax), static_cast<float*>(vinv),
+                                                  p.kv_heads, p.k_pad, p.k_pad, p.valid, ctx->num_sms, st);
+            if (e != cudaSuccess)
+                return cuda_fail("attention_sparse (V to fp16)", e);
+            ctx->launches += 2;
+        }
+        ctx->launches += 1;
+        return launched("attention_sparse (tcgen05)",
+                        mako::launch_attn_tc_sparse(p, dtype, sel_i32, v16, static_cast<const float*>(vinv), ctx->err,
+                                                    st));
+    }
     ctx->launches += 1;
-    return launched("attention_sparse",
-                    mako::launch_attn_mma(p, dtype, 128, true, sel_i32, static_cast<cudaStream_t>(stream)));
+    return launched("attention_sparse", mako::launch_attn_mma(p, dtype, 128, true, sel_i32, st));
 }
 
 } // namespace

@@ -141,8 +141,10 @@ def test_decode_zero_length_gives_zeros(ctx, oracle):
     assert C.within(got, want)[0]
 
 
-def sparse_fixture_run(ctx, oracle, dtype=0, topk=3, local=0, stride=0):
+def sparse_fixture_run(ctx, oracle, dtype=0, topk=3, local=0, stride=0, kernel=0):
     import torch
+    import mako_attn
+    ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, kernel)
     fx = oracle.sparse_test_fixture()
     q, k, v = dev(fx["q"], dtype), dev(fx["k"], dtype), dev(fx["v"], dtype)
     cnt = dev_raw(fx["cnt"])
@@ -156,10 +158,12 @@ def sparse_fixture_run(ctx, oracle, dtype=0, topk=3, local=0, stride=0):
     return fx, sel, nsel, o.cpu().numpy()
 
 
-def test_sparse_reference_fixture(ctx, oracle):
+@pytest.mark.parametrize("kernel", [0, 1], ids=["auto", "mma"])
+def test_sparse_reference_fixture(ctx, oracle, kernel):
     """tests/sparse_attn_test.cpp re-run through the C ABI: selection exact (vs the fp32 restatement and the
     reference's double procedure), attention within tolerance, unmapped rows untouched."""
-    fx, sel, nsel, o = sparse_fixture_run(ctx, oracle)
+    fx, sel, nsel, o = sparse_fixture_run(ctx, oracle, kernel=kernel)
+    assert ctx.device_error() == 0
     want_sel, want_nsel, *_ = oracle.cube_select(0, fx["q"], fx["k"], 2, 448, 512, 6, fx["cnt"], 3, mode=1)
     dbl_sel, *_ = oracle.cube_select(0, fx["q"], fx["k"], 2, 448, 512, 6, fx["cnt"], 3, mode=0)
     np.testing.assert_array_equal(sel, want_sel)
@@ -202,9 +206,12 @@ def test_cube_select_large_bit_exact(ctx, oracle):
         np.testing.assert_array_equal(sel, want)
 
 
-def test_block_sparse_lists(ctx, oracle):
+@pytest.mark.parametrize("kernel", [0, 1], ids=["auto", "mma"])
+def test_block_sparse_lists(ctx, oracle, kernel):
     """Config 4's mask format (int32 sorted kept-block lists + counts) at a reduced length."""
     import torch
+    import mako_attn
+    ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, kernel)
     heads, n, dtype = 4, 2048, 1
     nb = n // 64
     lists, counts = C.block_lists(40, heads, nb, 0.15)
@@ -222,6 +229,83 @@ def test_block_sparse_lists(ctx, oracle):
     ok, stats = C.within(got, want)
     assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
     assert np.all(got[3 * 64:4 * 64, 128:256] == 0.0)
+    assert ctx.device_error() == 0
+    ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 0)
+
+
+def h3_layout(seed, frames, ph, pw, dense, heads, kv_heads, dtype):
+    """A cube layout built the way H3::begin builds it (src/models/h3.cpp:510-546): 4x4x4 cubes over (frame, patch
+    row, patch column) with partial cubes at the grid edges (their rows scattered, not leading), then the dense rows;
+    map sends each tile row to its model row (video rows after the dense ones)."""
+    rng = np.random.default_rng(seed)
+    fc, yc, xc = -(-frames // 4), -(-ph // 4), -(-pw // 4)
+    n_cubes = fc * yc * xc
+    vrows = n_cubes * 64
+    rows = vrows + dense
+    q_pad, k_pad = C.round_up(rows, 64), C.round_up(rows, 128)
+    valid = np.zeros(k_pad, np.uint8)
+    map_ = np.full(q_pad, -1, np.int32)
+    cnt = np.zeros(n_cubes, np.uint32)
+    for f in range(frames):
+        for y in range(ph):
+            for x in range(pw):
+                cube = ((f // 4) * yc + y // 4) * xc + x // 4
+                r = cube * 64 + ((f % 4) * 4 + y % 4) * 4 + x % 4
+                map_[r] = dense + (f * ph + y) * pw + x
+                valid[r] = 1
+                cnt[cube] += 1
+    for r in range(dense):
+        map_[vrows + r] = r
+        valid[vrows + r] = 1
+    x = C.normal(rng, (3, max(heads, kv_heads), k_pad, 128)) * valid[None, None, :, None]
+    q = oracle_bits(x[0, :heads, :q_pad], dtype)
+    k = oracle_bits(x[1, :kv_heads], dtype)
+    v = oracle_bits(x[2, :kv_heads], dtype)
+    n_out = dense + frames * ph * pw
+    return dict(q=q, k=k, v=v, valid=valid, map=map_, cnt=cnt, n_cubes=n_cubes, rows=rows, q_pad=q_pad,
+                k_pad=k_pad, dense0=vrows, dense1=rows, n_out=n_out, heads=heads, kv_heads=kv_heads, dtype=dtype)
+
+
+def oracle_bits(x, dtype):
+    import oracle as O
+    return O.to_bits(x, dtype)
+
+
+@pytest.mark.parametrize("kernel", [0, 1], ids=["auto", "mma"])
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_sparse_h3_layout(ctx, oracle, kernel, dtype):
+    """Odd cube count (a tile half with no cube), partial edge cubes, dense rows, a permuted output map, GQA, the
+    local option -- cube_select then attention_sparse against the oracle."""
+    import torch
+    import mako_attn
+    L = h3_layout(70 + dtype, frames=3, ph=10, pw=10, dense=100, heads=4, kv_heads=2, dtype=dtype)
+    assert L["n_cubes"] % 2 == 1
+    topk = 3
+    q, k, v = dev(L["q"], dtype), dev(L["k"], dtype), dev(L["v"], dtype)
+    # cube_select pools q and k of the same head, so it runs on a kv-head-wide copy of q's first heads
+    sel_t, nsel_t = ctx.cube_select(q[:2], k, 2, L["q_pad"], L["k_pad"], L["n_cubes"], dev_raw(L["cnt"]), topk, 1, 0)
+    sel2 = sel_t.cpu().numpy().view(np.uint16)
+    want_sel, *_ = oracle.cube_select(dtype, L["q"][:2], L["k"], 2, L["q_pad"], L["k_pad"], L["n_cubes"], L["cnt"],
+                                      topk, local=1, mode=1)
+    np.testing.assert_array_equal(sel2, want_sel)
+    # per-head selection for all 4 q heads: heads 2, 3 reuse heads 0, 1's lists (any list is a valid input)
+    sel = np.concatenate([sel2, sel2], axis=0)
+    nsel = np.concatenate([nsel_t.cpu().numpy().view(np.uint16)] * 2, axis=0)
+    ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, kernel)
+    width = 4 * 128
+    o = torch.full((L["n_out"] + 3, width), SENTINEL, dtype=torch.float32, device="cuda")
+    ctx.attention_sparse(q, k, v, o, L["rows"], L["q_pad"], L["rows"], L["k_pad"], 4, 2, width, L["n_cubes"], topk,
+                         L["dense0"], L["dense1"], dev_raw(sel), dev_raw(nsel), dev_raw(L["valid"]), dev_raw(L["map"]))
+    torch.cuda.synchronize()
+    ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 0)
+    assert ctx.device_error() == 0
+    got = o.cpu().numpy()
+    want = np.full((L["n_out"] + 3, width), SENTINEL, np.float32)
+    oracle.attention_sparse(dtype, L["q"], L["k"], L["v"], L["rows"], L["q_pad"], L["rows"], L["k_pad"], 4, 2, width,
+                            L["n_cubes"], topk, L["dense0"], L["dense1"], sel, nsel, L["valid"], L["map"], out=want)
+    ok, stats = C.within(got[:L["n_out"]], want[:L["n_out"]])
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+    assert np.all(got[L["n_out"]:] == SENTINEL)
 
 
 def test_tcgen05_rejects_other_widths(ctx):
