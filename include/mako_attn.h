@@ -41,7 +41,10 @@ enum {
      * 2 the tcgen05 kernel (MAKO_ENOTSUP where it cannot run). */
     MAKO_OPT_PREFILL_KERNEL = 1,
     /* 1 (default): mako_attention with n_q == 1 runs the split-KV decode kernel; 0: the prefill kernel. */
-    MAKO_OPT_DECODE_ROUTE = 2
+    MAKO_OPT_DECODE_ROUTE = 2,
+    /* Keys per split of the decode kernel: 0 (default) chooses from the longest sequence and the SM count; else a
+     * multiple of 64 (raised when a sequence would need more than 1024 splits). */
+    MAKO_OPT_DECODE_CHUNK = 3
 };
 
 typedef struct mako_attn_ctx mako_attn_ctx;

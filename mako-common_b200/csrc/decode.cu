@@ -7,8 +7,10 @@
 // kv head's GQA group (up to 16 a CTA) from one read of K and V.  64-key tiles of K and V stream through a 3-stage
 // cp.async ring of 128-bit loads into XOR-swizzled shared memory; each of the 4 warps takes 16 keys of a tile on
 // mma.sync (the group's q rows padded to 16), keeps its own running softmax and accumulator, and the warps merge at
-// the end into one partial (o unnormalised, max, sum) per (sequence, head, split).
-// Kernel 2 (decode_combine_kernel): the log-sum-exp merge of a row's splits into o.
+// the end into one partial (o unnormalised, max, sum) per (sequence, head, split); a sequence with one split writes
+// o directly.
+// Kernel 2 (decode_combine_kernel): the log-sum-exp merge of a row's splits into o, launched as a programmatic
+// dependent of kernel 1 so that its launch overlaps kernel 1's last wave.
 #include "common.cuh"
 #include "kernels.h"
 #include "mako_attn.h"
@@ -20,6 +22,7 @@ namespace mako {
 namespace {
 
 constexpr int DBN = 64, DNT = 128, DST = 3, QR = 16;
+constexpr uint64_t kMaxSplits = 1024;
 
 template <int D, typename T>
 __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams p)
@@ -31,13 +34,18 @@ __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3, mi = lane >> 3;
     const uint32_t group = p.heads / p.kv_heads, rb = (group + QR - 1) / QR;
     const uint32_t b = blockIdx.z, kvh = blockIdx.y / rb, rblk = blockIdx.y % rb, split = blockIdx.x;
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");  // the combine may be scheduled now
     const int32_t lraw = p.kv_len ? p.kv_len[b] : int32_t(p.len);
     const uint32_t L = lraw > 0 ? uint32_t(lraw) : 0u;
     const uint32_t start = split * p.chunk;
-    if (start >= L)
-        return;
-    const uint32_t end = min(L, start + p.chunk);
     const uint32_t h0 = kvh * group + rblk * QR, nrows = min(uint32_t(QR), group - rblk * QR);
+    if (start >= L) {
+        if (L == 0 && split == 0)  // no key: the rows are 0
+            for (uint32_t i = tid; i < nrows * D; i += DNT)
+                p.o[uint64_t(b) * p.o_bstride + uint64_t(h0 + i / D) * D + i % D] = 0.0f;
+        return;
+    }
+    const uint32_t end = min(L, start + p.chunk);
     const T* qg = static_cast<const T*>(p.q) + uint64_t(b) * p.q_bstride;
     const T* kg = static_cast<const T*>(p.k) + uint64_t(b) * p.k_bstride + uint64_t(kvh) * p.k_hstride;
     const T* vg = static_cast<const T*>(p.v) + uint64_t(b) * p.k_bstride + uint64_t(kvh) * p.k_hstride;
@@ -180,6 +188,7 @@ __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams
                 make_float2(acc[i][2 * r], acc[i][2 * r + 1]);
     }
     __syncthreads();
+    const uint32_t ns = (L + p.chunk - 1) / p.chunk;  // this sequence's splits
     for (uint32_t i = tid; i < nrows * D; i += DNT) {
         const uint32_t r = i / D, d = i % D;
         float M = -INFINITY;
@@ -194,32 +203,80 @@ __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams
             Ls += sm[(w * 2 + 1) * QR + r] * fw;
             O += so[(w * QR + r) * D + d] * fw;
         }
-        const uint64_t row = (uint64_t(b) * p.heads + h0 + r) * p.n_splits + split;
-        p.o_part[row * D + d] = O;
-        if (d == 0)
-            p.ml_part[row] = make_float2(M, Ls);
+        if (ns == 1) {
+            p.o[uint64_t(b) * p.o_bstride + uint64_t(h0 + r) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
+        } else {
+            const uint64_t row = (uint64_t(b) * p.heads + h0 + r) * p.n_splits + split;
+            p.o_part[row * D + d] = O;
+            if (d == 0)
+                p.ml_part[row] = make_float2(M, Ls);
+        }
     }
 }
 
+// One CTA per (head, sequence), one thread per output value; the splits' weights 2^(m_s - M) go through shared
+// memory so each thread's loop is a stream of independent loads.
 template <int D>
 __global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p)
 {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");  // kernel 1's writes are visible from here on
+    __shared__ float w[kMaxSplits];
+    __shared__ float tot;
     const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int32_t lraw = p.kv_len ? p.kv_len[b] : int32_t(p.len);
     const uint32_t L = lraw > 0 ? uint32_t(lraw) : 0u;
     const uint32_t ns = min((L + p.chunk - 1) / p.chunk, p.n_splits);
+    if (ns <= 1)  // written by kernel 1 (one split, or no key)
+        return;
     const uint64_t row0 = (uint64_t(b) * p.heads + h) * p.n_splits;
     float M = -INFINITY;
-    for (uint32_t s = 0; s < ns; ++s)
+    for (uint32_t s = d; s < ns; s += D)
         M = fmaxf(M, p.ml_part[row0 + s].x);
-    float Ls = 0.0f, O = 0.0f;
-    for (uint32_t s = 0; s < ns; ++s) {
+    __shared__ float red[D / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if ((d & 31) == 0)
+        red[d >> 5] = M;
+    __syncthreads();
+    M = red[0];
+#pragma unroll
+    for (int i = 1; i < D / 32; ++i)
+        M = fmaxf(M, red[i]);
+    float ls = 0.0f;
+    for (uint32_t s = d; s < ns; s += D) {
         const float2 ml = p.ml_part[row0 + s];
         const float f = ml.x == -INFINITY ? 0.0f : ex2(ml.x - M);
-        Ls += ml.y * f;
-        O += p.o_part[(row0 + s) * D + d] * f;
+        w[s] = f;
+        ls += ml.y * f;
     }
-    p.o[uint64_t(b) * p.o_bstride + uint64_t(h) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    __syncthreads();
+    if ((d & 31) == 0)
+        red[d >> 5] = ls;
+    __syncthreads();
+    if (d == 0) {
+        float t = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i)
+            t += red[i];
+        tot = t;
+    }
+    __syncthreads();
+    const float* src = p.o_part + row0 * D + d;
+    float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    uint32_t s = 0;
+    for (; s + 8 <= ns; s += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            acc[u] += src[uint64_t(s + u) * D] * w[s + u];
+    }
+    for (; s < ns; ++s)
+        acc[0] += src[uint64_t(s) * D] * w[s];
+    const float O = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+    p.o[uint64_t(b) * p.o_bstride + uint64_t(h) * D + d] = tot > 0.0f ? O / tot : 0.0f;
 }
 
 template <int D, typename T>
@@ -233,17 +290,24 @@ cudaError_t launch_dec(const DecodeParams& p, cudaStream_t st)
         return e;
     const uint32_t group = p.heads / p.kv_heads, rb = (group + QR - 1) / QR;
     kern<<<dim3(p.n_splits, p.kv_heads * rb, p.batch), DNT, smem, st>>>(p);
-    e = cudaGetLastError();
-    if (e != cudaSuccess)
+    if ((e = cudaGetLastError()) != cudaSuccess)
         return e;
-    decode_combine_kernel<D><<<dim3(p.heads, p.batch), D, 0, st>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.heads, p.batch);
+    cfg.blockDim = dim3(D);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_combine_kernel<D>, p);
 }
 
 } // namespace
 
-void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t heads, int num_sms, uint32_t* chunk,
-                 uint32_t* n_splits)
+void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t heads, int num_sms, uint32_t chunk_opt,
+                 uint32_t* chunk, uint32_t* n_splits)
 {
     // Small chunks keep the tail short (the hardware scheduler back-fills freed SMs); at least ~8 CTAs an SM.
     const uint32_t group = heads / kv_heads, rb = (group + QR - 1) / QR;
@@ -252,6 +316,11 @@ void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t h
     uint64_t c = (rows + target - 1) / target;
     c = (c + DBN - 1) / DBN * DBN;
     c = c < 256 ? 256 : (c > 1024 ? 1024 : c);
+    if (chunk_opt)
+        c = chunk_opt;
+    if (uint64_t(max_len) > c * kMaxSplits)  // the combine's weight table holds kMaxSplits splits a row
+        c = (uint64_t(max_len) + kMaxSplits - 1) / kMaxSplits;
+    c = (c + DBN - 1) / DBN * DBN;
     *chunk = uint32_t(c);
     *n_splits = max_len ? uint32_t((max_len + c - 1) / c) : 1u;
 }
@@ -340,14 +409,17 @@ extern "C" int mako_attention_decode_noalloc(void* stream, int dtype, const void
 
     // The split plan of mako_attention_decode, with larger chunks when its partials would not fit the array.
     uint32_t chunk, n_splits;
-    mako::decode_plan(max_kv_len, batch, kv_heads, heads, sms, &chunk, &n_splits);
-    const uint64_t per_split = uint64_t(batch) * heads * (uint64_t(dim) * 4 + 8);
-    if (per_split > kNoAllocScratchBytes)
+    mako::decode_plan(max_kv_len, batch, kv_heads, heads, sms, 0, &chunk, &n_splits);
+    // Layout in the array: o partials, then (max, sum) partials.
+    auto bytes_for = [&](uint64_t ns) {
+        return (uint64_t(batch) * heads * ns * dim * 4 + 255) / 256 * 256 + uint64_t(batch) * heads * ns * 8;
+    };
+    if (bytes_for(1) > kNoAllocScratchBytes)
         return set_error(MAKO_EINVAL,
                          "decode_noalloc: %u sequences x %u heads of %u need %llu bytes of partials, beyond the %zu-byte "
                          "static scratch (use mako_attention_decode)",
-                         batch, heads, dim, (unsigned long long)per_split, kNoAllocScratchBytes);
-    while (uint64_t(n_splits) * per_split > kNoAllocScratchBytes) {
+                         batch, heads, dim, (unsigned long long)bytes_for(1), kNoAllocScratchBytes);
+    while (bytes_for(n_splits) > kNoAllocScratchBytes) {
         chunk += 64;
         n_splits = max_kv_len ? (max_kv_len + chunk - 1) / chunk : 1u;
     }
@@ -373,6 +445,7 @@ extern "C" int mako_attention_decode_noalloc(void* stream, int dtype, const void
     p.chunk = chunk;
     p.n_splits = n_splits;
     p.scale = 1.0f / sqrtf(float(dim));
+    // Every partial the combine reads is written by the same call first, so nothing in the array needs clearing.
     const size_t o_bytes = (size_t(batch) * heads * n_splits * dim * 4 + 255) / 256 * 256;
     p.o_part = static_cast<float*>(base);
     p.ml_part = reinterpret_cast<float2*>(static_cast<unsigned char*>(base) + o_bytes);

@@ -59,9 +59,10 @@ struct DecodeParams {
     uint32_t batch, heads, kv_heads, chunk, n_splits;
     float scale;
 };
-// Keys a split takes and how many splits, for the longest sequence max_len.
-void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t heads, int num_sms, uint32_t* chunk,
-                 uint32_t* n_splits);
+// Keys a split takes and how many splits, for the longest sequence max_len (chunk_opt: 0 automatic, else the
+// requested multiple of 64).
+void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t heads, int num_sms, uint32_t chunk_opt,
+                 uint32_t* chunk, uint32_t* n_splits);
 cudaError_t launch_decode(const DecodeParams& p, int dtype, int dim, cudaStream_t s);
 
 // cube_select: pooled means, their scores, the top k per (head, query cube).

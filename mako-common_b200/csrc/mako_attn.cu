@@ -20,6 +20,7 @@ struct mako_attn_ctx {
     int* err = nullptr;      // device flag the pipelined kernels set when a wait times out
     int prefill_kernel = 0;  // MAKO_OPT_PREFILL_KERNEL
     int decode_route = 1;    // MAKO_OPT_DECODE_ROUTE
+    uint32_t decode_chunk = 0;  // MAKO_OPT_DECODE_CHUNK
     uint64_t launches = 0;   // kernels enqueued
     struct Buf {
         void* ptr = nullptr;
@@ -195,6 +196,11 @@ int mako_attn_set_option(mako_attn_ctx* ctx, int option, int64_t value)
     case MAKO_OPT_DECODE_ROUTE:
         ctx->decode_route = value != 0;
         return MAKO_OK;
+    case MAKO_OPT_DECODE_CHUNK:
+        if (value < 0 || value % 64 || value > (int64_t(1) << 30))
+            return fail(MAKO_EINVAL, "decode chunk %lld (0 or a multiple of 64)", (long long)value);
+        ctx->decode_chunk = uint32_t(value);
+        return MAKO_OK;
     default:
         return fail(MAKO_EINVAL, "option %d", option);
     }
@@ -267,7 +273,7 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
         p.heads = heads;
         p.kv_heads = kv_heads;
         p.scale = 1.0f / sqrtf(float(dim));
-        mako::decode_plan(len, 1, kv_heads, heads, ctx->num_sms, &p.chunk, &p.n_splits);
+        mako::decode_plan(len, 1, kv_heads, heads, ctx->num_sms, ctx->decode_chunk, &p.chunk, &p.n_splits);
         void *op, *mlp;
         if (int rc = scratch(ctx, "dec_o", size_t(heads) * p.n_splits * dim * 4, &op))
             return rc;
@@ -355,7 +361,7 @@ int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const voi
     p.heads = heads;
     p.kv_heads = kv_heads;
     p.scale = 1.0f / sqrtf(float(dim));
-    mako::decode_plan(max_kv_len, batch, kv_heads, heads, ctx->num_sms, &p.chunk, &p.n_splits);
+    mako::decode_plan(max_kv_len, batch, kv_heads, heads, ctx->num_sms, ctx->decode_chunk, &p.chunk, &p.n_splits);
     void *op, *mlp;
     if (int rc = scratch(ctx, "dec_o", size_t(batch) * heads * p.n_splits * dim * 4, &op))
         return rc;

@@ -132,6 +132,21 @@ def test_decode(ctx, oracle, name, kw):
     assert ok, f"{name}: max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
 
 
+@pytest.mark.parametrize("chunk", [64, 256, 2048])
+def test_decode_split_lengths(ctx, oracle, chunk):
+    """The same result whatever the split length (many splits through the combine, or one split a sequence)."""
+    import mako_attn
+    case = C.decode_case(seed=28, batch=4, heads=16, kv_heads=4, dim=128, lo=100, hi=9000, dtype=0)
+    ctx.set_option(mako_attn.OPT_DECODE_CHUNK, chunk)
+    try:
+        got = run_decode(ctx, case)
+    finally:
+        ctx.set_option(mako_attn.OPT_DECODE_CHUNK, 0)
+    want = oracle.decode(0, case["q"], case["k"], case["v"], case["kv_len"], 16, 4, 128, case["k_stride"])
+    ok, stats = C.within(got, want)
+    assert ok, f"chunk {chunk}: {stats}"
+
+
 def test_decode_zero_length_gives_zeros(ctx, oracle):
     case = C.decode_case(seed=27, batch=3, heads=4, kv_heads=2, dim=128, lo=10, hi=20, dtype=0)
     case["kv_len"][1] = 0
