@@ -44,7 +44,10 @@ enum {
     MAKO_OPT_DECODE_ROUTE = 2,
     /* Keys per split of the decode kernel: 0 (default) chooses from the longest sequence and the SM count; else a
      * multiple of 64 (raised when a sequence would need more than 1024 splits). */
-    MAKO_OPT_DECODE_CHUNK = 3
+    MAKO_OPT_DECODE_CHUNK = 3,
+    /* 1: every call also records a CUDA event pair around its main kernel (the attention or split kernel, not the
+     * bf16 V pre-pass, the decode combine or the group barriers) for mako_attn_kernel_times; 0 (default): none. */
+    MAKO_OPT_KERNEL_TIMING = 4
 };
 
 typedef struct mako_attn_ctx mako_attn_ctx;
@@ -61,6 +64,11 @@ int mako_attn_set_option(mako_attn_ctx* ctx, int option, int64_t value);
 /* Kernel launches this context has enqueued since it was created (a counter for profiling harnesses; the
  * reference's equivalent is its per-kernel telemetry, src/gpu/runtime.cpp:343-370). */
 int mako_attn_launches(mako_attn_ctx* ctx, uint64_t* out);
+/* Device time in milliseconds of each main kernel recorded since the last call (MAKO_OPT_KERNEL_TIMING), oldest
+ * first: up to `cap` values into ms, their count into *n; waits for the recorded kernels to finish and forgets them.
+ * A measurement hook for benchmarks; the reference's counterpart is its per-kernel GPU timestamps
+ * (src/gpu/runtime.cpp:343-370). */
+int mako_attn_kernel_times(mako_attn_ctx* ctx, float* ms, uint32_t cap, uint32_t* n);
 /* Reads and clears the context's device error flag (synchronising the device): nonzero when a pipelined kernel gave
  * up on a wait (its bounded spin ran out) and left its outputs incomplete.  No reference counterpart: the reference
  * learns of a failed command buffer in gpu::Runtime::finish (src/gpu/runtime.cpp:466-471). */
@@ -133,6 +141,69 @@ int mako_attention_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const voi
 int mako_attention_block_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k,
                                 const void* v, float* o, uint32_t n, uint32_t heads, uint32_t kv_heads,
                                 const int32_t* lists, const int32_t* counts, uint32_t max_list);
+
+/* ---- Multi-GPU: one process per GPU of one box, the peers' memory mapped through CUDA IPC ------------------------
+ * No reference counterpart: mako-common drives one Apple GPU.  BASELINE's sharded forms -- heads across GPUs with the
+ * outputs gathered, and one long sequence's KV cache across GPUs with a log-sum-exp combine -- are built from these.
+ * Every rank of a group makes the same collective calls (mako_attention_gather, mako_attention_decode_kv_sharded) in
+ * the same order; each call's device waits on the other ranks are bounded (about a second) and a timeout sets the
+ * context's device error flag (mako_attn_device_error) instead of hanging. */
+
+#define MAKO_MAX_RANKS 8
+
+/* An opaque 64-byte CUDA IPC memory handle (cudaIpcMemHandle_t), passed between processes by the caller. */
+typedef struct {
+    unsigned char bytes[64];
+} mako_ipc_handle;
+
+/* cudaMalloc on ctx's device of memory the other processes of this box can map, and its handle. */
+int mako_peer_alloc(mako_attn_ctx* ctx, size_t bytes, void** ptr, mako_ipc_handle* handle);
+int mako_peer_free(mako_attn_ctx* ctx, void* ptr);
+/* Maps another process's mako_peer_alloc buffer (cudaIpcOpenMemHandle with lazy peer access); *ptr addresses it from
+ * ctx's device.  mako_peer_close unmaps it. */
+int mako_peer_open(mako_attn_ctx* ctx, const mako_ipc_handle* handle, void** ptr);
+int mako_peer_close(mako_attn_ctx* ctx, void* ptr);
+
+typedef struct mako_attn_group mako_attn_group;
+/* This rank's member of a group of n_ranks (<= MAKO_MAX_RANKS) processes: an exchange area for barrier flags and
+ * decode rows (max_rows = the most (sequence, head) rows one decode call will exchange), zeroed, and its handle for the
+ * caller to hand to every other rank.  The group uses ctx (its device, scratch and error flag) until destroyed. */
+int mako_group_create(mako_attn_ctx* ctx, uint32_t rank, uint32_t n_ranks, uint32_t max_rows, mako_attn_group** out,
+                      mako_ipc_handle* handle);
+/* Maps the other ranks' areas: handles[r] is rank r's handle from mako_group_create (this rank's own entry is not
+ * read).  Call once, on every rank, before the first collective call. */
+int mako_group_connect(mako_attn_group* g, const mako_ipc_handle* handles);
+/* As mako_group_connect for ranks that share one process (one thread per GPU, peer access enabled by the caller):
+ * areas[r] is rank r's area as ctx's device addresses it (mako_group_area gives each rank's own). */
+int mako_group_connect_ptrs(mako_attn_group* g, void* const* areas);
+/* This rank's exchange area (device pointer) and its size in bytes. */
+int mako_group_area(mako_attn_group* g, void** area, size_t* bytes);
+int mako_group_destroy(mako_attn_group* g);
+
+/* Head-sharded attention with the output all-gather fused into the kernel: this rank holds heads
+ * [head0, head0 + heads) of a larger problem (q [heads][q_pad][128], k and v [kv_heads][k_pad][128], its shard,
+ * heads % kv_heads == 0) and stores each output row's slice (columns (head0 + h) * 128) into every rank's o:
+ * o_ranks is a host array of n_ranks device pointers as this process addresses them (its own o and the others' o
+ * mapped with mako_peer_open), each o [n_q][width] floats.  When this call's work on `stream` completes, this rank's
+ * o holds every rank's heads.  The call begins with a barrier (no rank writes into an o that its owner may still be
+ * reading from the previous call) and ends with one (every rank's stores have landed).  Masking as mako_attention
+ * (q_pos0, block); 128-wide heads on sm_100 only (MAKO_ENOTSUP otherwise).  Replaces, for one rank, what the
+ * reference's TransformerRuntime::attention (src/models/runtime.cpp:262-273) computes for all heads. */
+int mako_attention_gather(mako_attn_group* g, void* stream, int dtype, const void* q, const void* k, const void* v,
+                          float* const* o_ranks, uint32_t n_q, uint32_t q_pad, uint32_t n_k, uint32_t k_pad,
+                          uint32_t heads, uint32_t kv_heads, uint32_t head0, uint32_t q_pos0, uint32_t block,
+                          uint32_t width);
+
+/* KV-sharded decode: every rank holds the same queries q [batch][heads][dim] and its own share of each sequence's
+ * keys, k and v [batch][kv_heads][k_stride][dim] with kv_len [batch] (device int32, this rank's key count per
+ * sequence, at most max_kv_len); o [batch][heads * dim] receives on every rank the attention over all ranks' keys.
+ * Each rank merges its splits into one (o, max, sum) row per (sequence, head), stores it into every rank's exchange
+ * area over NVLink and merges all ranks' rows by log-sum-exp (one kernel after the split kernel).  batch * heads must
+ * be at most the group's max_rows.  Same element types and dims as mako_attention_decode. */
+int mako_attention_decode_kv_sharded(mako_attn_group* g, void* stream, int dtype, const void* q, const void* k,
+                                     const void* v, float* o, uint32_t batch, const int32_t* kv_len,
+                                     uint32_t max_kv_len, uint32_t heads, uint32_t kv_heads, uint32_t dim,
+                                     uint32_t k_stride);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -42,7 +42,9 @@ constexpr long long WAIT_LIMIT = 1ll << 31;             // clock cycles (~1 s) b
 
 struct __align__(64) TcParams {
     CUtensorMap tq, tk, tv;
-    float* o;
+    float* od[8];   // output destinations (this rank's o, then the peers' mapped o for the head-sharded form)
+    uint32_t n_od;  // destinations in od
+    uint32_t head0;  // column of local head h: (head0 + h) * 128
     int* err;
     const float* vinv;  // per kv head: 1 / (the fp16 copy's scale), null for fp16 inputs
     uint32_t qk_fmt;    // Q / K element format: 0 fp16, 1 bf16
@@ -327,7 +329,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             atomicExch(p.err, 3);
         const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
         const uint32_t grow = q0 + x * TBM + row;
-        float* orow = p.o + uint64_t(grow) * p.width + uint64_t(h) * TD;
+        const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(p.head0 + h) * TD;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -342,12 +344,21 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             }
             if (grow < p.n_q) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    *reinterpret_cast<float4*>(orow + c * 32 + i * 4) =
-                        make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                                    __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+                for (int i = 0; i < 32; ++i)
+                    o[i] = __float_as_uint(__uint_as_float(o[i]) * inv);
+                // Head-sharded form: the same row slice into every rank's o (NVLink stores to the peers).
+                for (uint32_t dI = 0; dI < p.n_od; ++dI) {
+                    float* orow = p.od[dI] + ooff;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        *reinterpret_cast<float4*>(orow + c * 32 + i * 4) =
+                            make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                        __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+                }
             }
         }
+        if (p.n_od > 1)  // the peers' copies are performed before this rank's barrier releases them
+            __threadfence_system();
     }
     __syncwarp();
     fence_before();
@@ -490,7 +501,18 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, const void* v16, cons
     if (!head_map(&p.tq, a.q, bf, a.q_pad, a.heads) || !head_map(&p.tk, a.k, bf, a.k_pad, a.kv_heads) ||
         !head_map(&p.tv, bf ? v16 : a.v, false, a.k_pad, a.kv_heads))
         return cudaErrorInvalidValue;
-    p.o = a.o;
+    if (a.n_od == 0) {
+        p.od[0] = a.o;
+        p.n_od = 1;
+        p.head0 = 0;
+    } else {
+        if (a.n_od > 8)
+            return cudaErrorInvalidValue;
+        for (uint32_t i = 0; i < a.n_od; ++i)
+            p.od[i] = a.od[i];
+        p.n_od = a.n_od;
+        p.head0 = a.head0;
+    }
     p.err = err;
     p.vinv = bf ? vinv : nullptr;
     p.qk_fmt = bf ? 1u : 0u;

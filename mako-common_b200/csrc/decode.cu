@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams
     const uint32_t start = split * p.chunk;
     const uint32_t h0 = kvh * group + rblk * QR, nrows = min(uint32_t(QR), group - rblk * QR);
     if (start >= L) {
-        if (L == 0 && split == 0)  // no key: the rows are 0
+        if (L == 0 && split == 0 && !p.keep_partials)  // no key: the rows are 0
             for (uint32_t i = tid; i < nrows * D; i += DNT)
                 p.o[uint64_t(b) * p.o_bstride + uint64_t(h0 + i / D) * D + i % D] = 0.0f;
         return;
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams
             Ls += sm[(w * 2 + 1) * QR + r] * fw;
             O += so[(w * QR + r) * D + d] * fw;
         }
-        if (ns == 1) {
+        if (ns == 1 && !p.keep_partials) {
             p.o[uint64_t(b) * p.o_bstride + uint64_t(h0 + r) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
         } else {
             const uint64_t row = (uint64_t(b) * p.heads + h0 + r) * p.n_splits + split;
@@ -304,7 +304,233 @@ cudaError_t launch_dec(const DecodeParams& p, cudaStream_t st)
     return cudaLaunchKernelEx(&cfg, decode_combine_kernel<D>, p);
 }
 
+template <int D, typename T>
+cudaError_t launch_split_only(const DecodeParams& p, cudaStream_t st)
+{
+    constexpr int smem = (QR + 2 * DST * DBN) * D * 2;
+    auto kern = decode_split_kernel<D, T>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess)
+        return e;
+    const uint32_t group = p.heads / p.kv_heads, rb = (group + QR - 1) / QR;
+    kern<<<dim3(p.n_splits, p.kv_heads * rb, p.batch), DNT, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+constexpr long long kXchgWaitLimit = 1ll << 31;  // clock cycles (~1 s) before a wait on a peer gives up
+
+// One CTA per (head, sequence), one thread per output value.  Phase 1 merges this rank's splits (as
+// decode_combine_kernel, but keeping the unnormalised sum and its maximum); phase 2 stores that row into slot `rank`
+// of every rank's area and releases the row's flag there; phase 3 waits until every rank's row has arrived in this
+// rank's area (bounded) and merges them by log-sum-exp into o.  The area is double-buffered by epoch parity: a rank
+// one call ahead writes the other half, and it cannot get two calls ahead because its own phase 3 waits for ours.
+template <int D>
+__global__ void __launch_bounds__(D) decode_xchg_kernel(const DecodeParams p, const XchgParams x)
+{
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    __shared__ float w[kMaxSplits];
+    __shared__ float red[D / 32];
+    __shared__ float tot;
+    __shared__ int timed_out;
+    const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const uint32_t row = b * p.heads + h, par = x.epoch & 1u;
+    const int32_t lraw = p.kv_len ? p.kv_len[b] : int32_t(p.len);
+    const uint32_t L = lraw > 0 ? uint32_t(lraw) : 0u;
+    const uint32_t ns = min((L + p.chunk - 1) / p.chunk, p.n_splits);
+    const uint64_t row0 = (uint64_t(b) * p.heads + h) * p.n_splits;
+    if (d == 0)
+        timed_out = 0;
+
+    // ---- phase 1: this rank's splits
+    float M = -INFINITY;
+    for (uint32_t s = d; s < ns; s += D)
+        M = fmaxf(M, p.ml_part[row0 + s].x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if ((d & 31) == 0)
+        red[d >> 5] = M;
+    __syncthreads();
+    M = red[0];
+#pragma unroll
+    for (int i = 1; i < D / 32; ++i)
+        M = fmaxf(M, red[i]);
+    float ls = 0.0f;
+    for (uint32_t s = d; s < ns; s += D) {
+        const float2 ml = p.ml_part[row0 + s];
+        const float f = ml.x == -INFINITY ? 0.0f : ex2(ml.x - M);
+        w[s] = f;
+        ls += ml.y * f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    __syncthreads();
+    if ((d & 31) == 0)
+        red[d >> 5] = ls;
+    __syncthreads();
+    if (d == 0) {
+        float t = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i)
+            t += red[i];
+        tot = t;
+    }
+    __syncthreads();
+    float O = 0.0f;
+    for (uint32_t s = 0; s < ns; ++s)
+        O += p.o_part[(row0 + s) * D + d] * w[s];
+    const float Ls = tot;
+
+    // ---- phase 2: push (O, M, Ls) into slot `rank` of every rank's area, then release the row's flags
+    const uint64_t xoff = xchg_rows_offset(x.rows_cap);
+    const uint64_t slot = ((uint64_t(par) * kMaxRanks + x.rank) * x.rows_cap + row) * kXchgStride;
+    for (uint32_t g = 0; g < x.n_ranks; ++g) {
+        float* dst = reinterpret_cast<float*>(x.area[g] + xoff) + slot;
+        dst[d] = O;
+        if (d == 0)
+            *reinterpret_cast<float2*>(dst + D) = make_float2(M, Ls);
+    }
+    __syncthreads();
+    const uint64_t fslot = (uint64_t(par) * kMaxRanks + x.rank) * x.rows_cap + row;
+    if (d < x.n_ranks) {
+        asm volatile("fence.acq_rel.sys;\n" ::: "memory");
+        st_release_sys(reinterpret_cast<uint32_t*>(x.area[d] + 256) + fslot, x.epoch);
+    }
+
+    // ---- phase 3: every rank's row in this rank's area, merged
+    if (d < x.n_ranks) {
+        const uint32_t* f = reinterpret_cast<const uint32_t*>(x.area[x.rank] + 256) +
+                            (uint64_t(par) * kMaxRanks + d) * x.rows_cap + row;
+        if (ld_acquire_sys(f) != x.epoch) {
+            const long long t0 = clock64();
+            while (ld_acquire_sys(f) != x.epoch)
+                if (clock64() - t0 > kXchgWaitLimit) {
+                    timed_out = 1;
+                    atomicExch(x.err, 31);
+                    break;
+                }
+        }
+    }
+    __syncthreads();
+    const float* mine = reinterpret_cast<const float*>(x.area[x.rank] + xoff);
+    float Mg = -INFINITY;
+    for (uint32_t g = 0; g < x.n_ranks; ++g)
+        Mg = fmaxf(Mg, __ldcg(mine + ((uint64_t(par) * kMaxRanks + g) * x.rows_cap + row) * kXchgStride + D));
+    float T = 0.0f, Og = 0.0f;
+    for (uint32_t g = 0; g < x.n_ranks; ++g) {
+        const float* src = mine + ((uint64_t(par) * kMaxRanks + g) * x.rows_cap + row) * kXchgStride;
+        const float mg = __ldcg(src + D);
+        const float f = mg == -INFINITY ? 0.0f : ex2(mg - Mg);
+        T += __ldcg(src + D + 1) * f;
+        Og += __ldcg(src + d) * f;
+    }
+    p.o[uint64_t(b) * p.o_bstride + uint64_t(h) * D + d] = (T > 0.0f && !timed_out) ? Og / T : 0.0f;
+}
+
+// Barrier over the group: thread g releases this rank's flag in rank g's area, then waits for rank g's flag in ours.
+__global__ void group_barrier_kernel(const XchgParams x, uint32_t kind)
+{
+    const uint32_t g = threadIdx.x, par = x.epoch & 1u;
+    if (g >= x.n_ranks)
+        return;
+    asm volatile("fence.acq_rel.sys;\n" ::: "memory");
+    st_release_sys(reinterpret_cast<uint32_t*>(x.area[g]) + (par * 2 + kind) * kMaxRanks + x.rank, x.epoch);
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(x.area[x.rank]) + (par * 2 + kind) * kMaxRanks + g;
+    if (ld_acquire_sys(f) != x.epoch) {
+        const long long t0 = clock64();
+        while (ld_acquire_sys(f) != x.epoch)
+            if (clock64() - t0 > kXchgWaitLimit) {
+                atomicExch(x.err, 30);
+                break;
+            }
+    }
+}
+
 } // namespace
+
+cudaError_t launch_decode_split(const DecodeParams& p, int dtype, int dim, cudaStream_t st)
+{
+    if (p.batch == 0 || p.heads == 0)
+        return cudaSuccess;
+    const bool bf = dtype == kBF16;
+    switch (dim) {
+    case 64:
+        return bf ? launch_split_only<64, __nv_bfloat16>(p, st) : launch_split_only<64, __half>(p, st);
+    case 128:
+        return bf ? launch_split_only<128, __nv_bfloat16>(p, st) : launch_split_only<128, __half>(p, st);
+    case 256:
+        return bf ? launch_split_only<256, __nv_bfloat16>(p, st) : launch_split_only<256, __half>(p, st);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_decode_combine(const DecodeParams& p, int dim, cudaStream_t st)
+{
+    if (p.batch == 0 || p.heads == 0)
+        return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.heads, p.batch);
+    cfg.blockDim = dim3(dim);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    switch (dim) {
+    case 64:
+        return cudaLaunchKernelEx(&cfg, decode_combine_kernel<64>, p);
+    case 128:
+        return cudaLaunchKernelEx(&cfg, decode_combine_kernel<128>, p);
+    case 256:
+        return cudaLaunchKernelEx(&cfg, decode_combine_kernel<256>, p);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_decode_xchg(const DecodeParams& p, const XchgParams& x, int dim, cudaStream_t st)
+{
+    if (p.batch == 0 || p.heads == 0)
+        return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.heads, p.batch);
+    cfg.blockDim = dim3(dim);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    switch (dim) {
+    case 64:
+        return cudaLaunchKernelEx(&cfg, decode_xchg_kernel<64>, p, x);
+    case 128:
+        return cudaLaunchKernelEx(&cfg, decode_xchg_kernel<128>, p, x);
+    case 256:
+        return cudaLaunchKernelEx(&cfg, decode_xchg_kernel<256>, p, x);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_group_barrier(const XchgParams& x, uint32_t kind, cudaStream_t st)
+{
+    group_barrier_kernel<<<1, 32, 0, st>>>(x, kind);
+    return cudaGetLastError();
+}
 
 void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t heads, int num_sms, uint32_t chunk_opt,
                  uint32_t* chunk, uint32_t* n_splits)

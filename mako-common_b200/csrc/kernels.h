@@ -27,6 +27,11 @@ struct AttnParams {
     const void* nsel;      // [heads][n_cubes], same integer type as sel
     const uint8_t* valid;  // [k_pad] key validity, null: every key valid
     const int32_t* map;    // [q_pad] output row per query row (< 0 dropped), null: identity
+    // Output destinations of the head-sharded form (tcgen05 dense kernel only): the same rows are stored into
+    // od[0 .. n_od) (this rank's o and the peers' mapped o), local head h at column (head0 + h) * dim.  n_od == 0:
+    // the single destination `o` at column h * dim.
+    float* od[8];
+    uint32_t n_od, head0;
 };
 
 // Portable flash attention on mma.sync tensor cores, any head width of 64 / 128 / 256.
@@ -58,12 +63,44 @@ struct DecodeParams {
     uint64_t q_bstride, q_hstride, k_bstride, k_hstride, o_bstride;  // in elements
     uint32_t batch, heads, kv_heads, chunk, n_splits;
     float scale;
+    uint32_t keep_partials;  // 1: always write partials (the KV-sharded combine reads them), never o
 };
 // Keys a split takes and how many splits, for the longest sequence max_len (chunk_opt: 0 automatic, else the
 // requested multiple of 64).
 void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t heads, int num_sms, uint32_t chunk_opt,
                  uint32_t* chunk, uint32_t* n_splits);
 cudaError_t launch_decode(const DecodeParams& p, int dtype, int dim, cudaStream_t s);
+
+// ---- multi-GPU exchange (one process per GPU, peers' memory mapped through CUDA IPC) ------------------------------
+
+constexpr uint32_t kMaxRanks = 8;
+constexpr uint32_t kXchgStride = 260;  // floats per exchanged decode row: o[dim <= 256], max, sum, 2 pad
+// Layout of a rank's exchange area (bytes from its base):
+//   0     barrier flags u32 [2 parities][2 kinds (enter, done)][kMaxRanks]
+//   256   decode row flags u32 [2][kMaxRanks][rows_cap]
+//   xoff  decode rows f32 [2][kMaxRanks][rows_cap][kXchgStride], xoff = 256 + 2 * kMaxRanks * rows_cap * 4 rounded
+//         up to 256
+__host__ __device__ inline uint64_t xchg_rows_offset(uint32_t rows_cap) { return (256 + uint64_t(2) * kMaxRanks * rows_cap * 4 + 255) / 256 * 256; }
+__host__ __device__ inline uint64_t xchg_bytes(uint32_t rows_cap)
+{
+    return xchg_rows_offset(rows_cap) + uint64_t(2) * kMaxRanks * rows_cap * kXchgStride * 4;
+}
+
+struct XchgParams {
+    unsigned char* area[kMaxRanks];  // every rank's exchange area as this process addresses it (area[rank]: own)
+    uint32_t n_ranks, rank, epoch, rows_cap;
+    int* err;
+};
+// Every rank signals the others and waits (bounded) until all have signalled `epoch` for barrier `kind`
+// (0 enter, 1 done); stream-ordered: work before it on every rank happens before work after it on any rank.
+cudaError_t launch_group_barrier(const XchgParams& x, uint32_t kind, cudaStream_t s);
+// KV-sharded decode, second half: merges this rank's splits per (sequence, head), pushes the row to every rank's
+// area, waits for all ranks' rows and merges them by log-sum-exp into o.
+cudaError_t launch_decode_xchg(const DecodeParams& p, const XchgParams& x, int dim, cudaStream_t s);
+// The two kernels of launch_decode one at a time: the splits (partials, or o for one-split sequences unless
+// p.keep_partials), then the log-sum-exp combine (a programmatic dependent of the split kernel).
+cudaError_t launch_decode_split(const DecodeParams& p, int dtype, int dim, cudaStream_t s);
+cudaError_t launch_decode_combine(const DecodeParams& p, int dim, cudaStream_t s);
 
 // cube_select: pooled means, their scores, the top k per (head, query cube).
 struct CubeParams {

@@ -12,6 +12,8 @@
 #include <new>
 #include <string>
 #include <unordered_map>
+#include <utility>
+#include <vector>
 
 struct mako_attn_ctx {
     int device = 0;
@@ -22,6 +24,9 @@ struct mako_attn_ctx {
     int decode_route = 1;    // MAKO_OPT_DECODE_ROUTE
     uint32_t decode_chunk = 0;  // MAKO_OPT_DECODE_CHUNK
     uint64_t launches = 0;   // kernels enqueued
+    bool timing = false;     // MAKO_OPT_KERNEL_TIMING
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;  // main-kernel event pairs, [0, used) recorded
+    size_t used = 0;
     struct Buf {
         void* ptr = nullptr;
         size_t bytes = 0;
@@ -112,6 +117,35 @@ int check_ctx(mako_attn_ctx* ctx, int dtype)
     return MAKO_OK;
 }
 
+// Brackets a call's main kernel with a recorded event pair when the context times kernels (no-op otherwise).
+struct KernelTimer {
+    mako_attn_ctx* ctx;
+    cudaStream_t st;
+    bool on = false;
+    KernelTimer(mako_attn_ctx* c, cudaStream_t s) : ctx(c), st(s)
+    {
+        if (!ctx->timing)
+            return;
+        if (ctx->used == ctx->events.size()) {
+            cudaEvent_t a, b;
+            if (cudaEventCreate(&a) != cudaSuccess)
+                return;
+            if (cudaEventCreate(&b) != cudaSuccess) {
+                cudaEventDestroy(a);
+                return;
+            }
+            ctx->events.emplace_back(a, b);
+        }
+        on = cudaEventRecord(ctx->events[ctx->used].first, st) == cudaSuccess;
+    }
+    void stop()
+    {
+        if (on && cudaEventRecord(ctx->events[ctx->used].second, st) == cudaSuccess)
+            ++ctx->used;
+        on = false;
+    }
+};
+
 int launched(const char* what, cudaError_t e)
 {
     if (e != cudaSuccess)
@@ -172,6 +206,10 @@ int mako_attn_destroy(mako_attn_ctx* ctx)
         DeviceGuard dg(ctx->device);
         if (ctx->err)
             cudaFree(ctx->err);
+        for (auto& ev : ctx->events) {
+            cudaEventDestroy(ev.first);
+            cudaEventDestroy(ev.second);
+        }
         for (auto& kv : ctx->scratch)
             if (kv.second.ptr) {
                 cudaError_t e = cudaFree(kv.second.ptr);
@@ -196,6 +234,9 @@ int mako_attn_set_option(mako_attn_ctx* ctx, int option, int64_t value)
     case MAKO_OPT_DECODE_ROUTE:
         ctx->decode_route = value != 0;
         return MAKO_OK;
+    case MAKO_OPT_KERNEL_TIMING:
+        ctx->timing = value != 0;
+        return MAKO_OK;
     case MAKO_OPT_DECODE_CHUNK:
         if (value < 0 || value % 64 || value > (int64_t(1) << 30))
             return fail(MAKO_EINVAL, "decode chunk %lld (0 or a multiple of 64)", (long long)value);
@@ -211,6 +252,30 @@ int mako_attn_launches(mako_attn_ctx* ctx, uint64_t* out)
     if (!ctx || !out)
         return fail(MAKO_EINVAL, "null argument");
     *out = ctx->launches;
+    return MAKO_OK;
+}
+
+int mako_attn_kernel_times(mako_attn_ctx* ctx, float* ms, uint32_t cap, uint32_t* n)
+{
+    if (!ctx || !n || (cap && !ms))
+        return fail(MAKO_EINVAL, "null argument");
+    DeviceGuard dg(ctx->device);
+    uint32_t k = 0;
+    for (size_t i = 0; i < ctx->used; ++i) {
+        float t = 0.0f;
+        cudaError_t e = cudaEventSynchronize(ctx->events[i].second);
+        if (e == cudaSuccess)
+            e = cudaEventElapsedTime(&t, ctx->events[i].first, ctx->events[i].second);
+        if (e != cudaSuccess) {
+            ctx->used = 0;
+            return cuda_fail("kernel times", e);
+        }
+        if (k < cap)
+            ms[k] = t;
+        ++k;
+    }
+    ctx->used = 0;
+    *n = k;
     return MAKO_OK;
 }
 
@@ -282,7 +347,12 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
         p.o_part = static_cast<float*>(op);
         p.ml_part = static_cast<float2*>(mlp);
         ctx->launches += 2;
-        return launched("attention (decode)", mako::launch_decode(p, dtype, dim, st));
+        KernelTimer t(ctx, st);
+        cudaError_t e = mako::launch_decode_split(p, dtype, int(dim), st);
+        t.stop();
+        if (e != cudaSuccess)
+            return cuda_fail("attention (decode splits)", e);
+        return launched("attention (decode combine)", mako::launch_decode_combine(p, int(dim), st));
     }
     mako::AttnParams p{};
     p.q = q;
@@ -319,11 +389,16 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
             ctx->launches += 2;
         }
         ctx->launches += 1;
-        return launched("attention (tcgen05)",
-                        mako::launch_attn_tc(p, dtype, v16, static_cast<const float*>(vinv), ctx->err, st));
+        KernelTimer t(ctx, st);
+        cudaError_t e = mako::launch_attn_tc(p, dtype, v16, static_cast<const float*>(vinv), ctx->err, st);
+        t.stop();
+        return launched("attention (tcgen05)", e);
     }
     ctx->launches += 1;
-    return launched("attention", mako::launch_attn_mma(p, dtype, dim, false, false, st));
+    KernelTimer t(ctx, st);
+    cudaError_t e = mako::launch_attn_mma(p, dtype, dim, false, false, st);
+    t.stop();
+    return launched("attention", e);
 }
 
 int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v,
@@ -370,7 +445,13 @@ int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const voi
     p.o_part = static_cast<float*>(op);
     p.ml_part = static_cast<float2*>(mlp);
     ctx->launches += 2;
-    return launched("decode", mako::launch_decode(p, dtype, dim, static_cast<cudaStream_t>(stream)));
+    auto st = static_cast<cudaStream_t>(stream);
+    KernelTimer t(ctx, st);
+    cudaError_t e = mako::launch_decode_split(p, dtype, int(dim), st);
+    t.stop();
+    if (e != cudaSuccess)
+        return cuda_fail("decode (splits)", e);
+    return launched("decode (combine)", mako::launch_decode_combine(p, int(dim), st));
 }
 
 int mako_cube_select(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, uint32_t heads,
@@ -451,12 +532,17 @@ int sparse_common(mako_attn_ctx* ctx, void* stream, int dtype, mako::AttnParams&
             ctx->launches += 2;
         }
         ctx->launches += 1;
-        return launched("attention_sparse (tcgen05)",
-                        mako::launch_attn_tc_sparse(p, dtype, sel_i32, v16, static_cast<const float*>(vinv), ctx->err,
-                                                    st));
+        KernelTimer t(ctx, st);
+        cudaError_t e = mako::launch_attn_tc_sparse(p, dtype, sel_i32, v16, static_cast<const float*>(vinv), ctx->err,
+                                                    st);
+        t.stop();
+        return launched("attention_sparse (tcgen05)", e);
     }
     ctx->launches += 1;
-    return launched("attention_sparse", mako::launch_attn_mma(p, dtype, 128, true, sel_i32, st));
+    KernelTimer t(ctx, st);
+    cudaError_t e = mako::launch_attn_mma(p, dtype, 128, true, sel_i32, st);
+    t.stop();
+    return launched("attention_sparse", e);
 }
 
 } // namespace
@@ -540,6 +626,366 @@ int mako_attention_block_sparse(mako_attn_ctx* ctx, void* stream, int dtype, con
     p.valid = nullptr;
     p.map = nullptr;
     return sparse_common(ctx, stream, dtype, p, true);
+}
+
+} // extern "C"
+
+// ---- multi-GPU ------------------------------------------------------------------------------------------------------
+
+struct mako_attn_group {
+    mako_attn_ctx* ctx = nullptr;
+    uint32_t rank = 0, n_ranks = 1, rows_cap = 0;
+    void* area = nullptr;                     // this rank's exchange area
+    void* peer[MAKO_MAX_RANKS] = {};          // every rank's area as this process addresses it
+    bool connected = false;
+    bool mapped = false;                      // peers opened through IPC (closed on destroy)
+    uint32_t epoch = 0;                       // collective calls so far (flags carry the call's number)
+};
+
+namespace {
+
+static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(mako_ipc_handle), "IPC handle size");
+static_assert(MAKO_MAX_RANKS == mako::kMaxRanks, "rank limit");
+
+mako::XchgParams xchg_params(mako_attn_group* g)
+{
+    mako::XchgParams x{};
+    for (uint32_t r = 0; r < g->n_ranks; ++r)
+        x.area[r] = static_cast<unsigned char*>(g->peer[r]);
+    x.n_ranks = g->n_ranks;
+    x.rank = g->rank;
+    if (++g->epoch == 0)  // 0 is the flags' initial value: never a call's number
+        g->epoch = 1;
+    x.epoch = g->epoch;
+    x.rows_cap = g->rows_cap;
+    x.err = g->ctx->err;
+    return x;
+}
+
+int check_group(mako_attn_group* g, int dtype)
+{
+    if (!g)
+        return fail(MAKO_EINVAL, "null group");
+    if (!g->connected)
+        return fail(MAKO_EINVAL, "group not connected (mako_group_connect)");
+    return check_ctx(g->ctx, dtype);
+}
+
+} // namespace
+
+extern "C" {
+
+int mako_peer_alloc(mako_attn_ctx* ctx, size_t bytes, void** ptr, mako_ipc_handle* handle)
+{
+    if (!ctx || !ptr || !handle || !bytes)
+        return fail(MAKO_EINVAL, "peer_alloc: null argument or zero bytes");
+    *ptr = nullptr;
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MAKO_ENOMEM, "peer_alloc: %zu bytes: %s", bytes, cudaGetErrorString(e));
+    }
+    cudaIpcMemHandle_t h;
+    if ((e = cudaIpcGetMemHandle(&h, p)) != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail("peer_alloc: cudaIpcGetMemHandle", e);
+    }
+    std::memcpy(handle->bytes, &h, sizeof(h));
+    *ptr = p;
+    g_error.clear();
+    return MAKO_OK;
+}
+
+int mako_peer_free(mako_attn_ctx* ctx, void* ptr)
+{
+    if (!ctx)
+        return fail(MAKO_EINVAL, "peer_free: null context");
+    if (!ptr)
+        return MAKO_OK;
+    DeviceGuard dg(ctx->device);
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? (g_error.clear(), MAKO_OK) : cuda_fail("peer_free", e);
+}
+
+int mako_peer_open(mako_attn_ctx* ctx, const mako_ipc_handle* handle, void** ptr)
+{
+    if (!ctx || !handle || !ptr)
+        return fail(MAKO_EINVAL, "peer_open: null argument");
+    *ptr = nullptr;
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        *ptr = nullptr;
+        cudaGetLastError();
+        return cuda_fail("peer_open: cudaIpcOpenMemHandle", e);
+    }
+    g_error.clear();
+    return MAKO_OK;
+}
+
+int mako_peer_close(mako_attn_ctx* ctx, void* ptr)
+{
+    if (!ctx)
+        return fail(MAKO_EINVAL, "peer_close: null context");
+    if (!ptr)
+        return MAKO_OK;
+    DeviceGuard dg(ctx->device);
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? (g_error.clear(), MAKO_OK) : cuda_fail("peer_close", e);
+}
+
+int mako_group_create(mako_attn_ctx* ctx, uint32_t rank, uint32_t n_ranks, uint32_t max_rows, mako_attn_group** out,
+                      mako_ipc_handle* handle)
+{
+    if (!ctx || !out || !handle)
+        return fail(MAKO_EINVAL, "group_create: null argument");
+    *out = nullptr;
+    if (n_ranks == 0 || n_ranks > MAKO_MAX_RANKS || rank >= n_ranks)
+        return fail(MAKO_EINVAL, "group_create: rank %u of %u (at most %d ranks)", rank, n_ranks, MAKO_MAX_RANKS);
+    if (max_rows == 0 || max_rows > (1u << 20))
+        return fail(MAKO_EINVAL, "group_create: max_rows %u (1 .. 2^20)", max_rows);
+    auto* g = new (std::nothrow) mako_attn_group;
+    if (!g)
+        return fail(MAKO_ENOMEM, "group");
+    g->ctx = ctx;
+    g->rank = rank;
+    g->n_ranks = n_ranks;
+    g->rows_cap = max_rows;
+    const size_t bytes = mako::xchg_bytes(max_rows);
+    if (int rc = mako_peer_alloc(ctx, bytes, &g->area, handle)) {
+        delete g;
+        return rc;
+    }
+    {
+        DeviceGuard dg(ctx->device);
+        cudaError_t e = cudaMemset(g->area, 0, bytes);
+        if (e == cudaSuccess)
+            e = cudaDeviceSynchronize();  // zeroed before any peer can map and signal into it
+        if (e != cudaSuccess) {
+            cudaFree(g->area);
+            delete g;
+            return cuda_fail("group_create: clear", e);
+        }
+    }
+    g->peer[rank] = g->area;
+    *out = g;
+    g_error.clear();
+    return MAKO_OK;
+}
+
+int mako_group_connect(mako_attn_group* g, const mako_ipc_handle* handles)
+{
+    if (!g || !handles)
+        return fail(MAKO_EINVAL, "group_connect: null argument");
+    if (g->connected)
+        return fail(MAKO_EINVAL, "group_connect: already connected");
+    for (uint32_t r = 0; r < g->n_ranks; ++r) {
+        if (r == g->rank)
+            continue;
+        if (int rc = mako_peer_open(g->ctx, &handles[r], &g->peer[r])) {
+            for (uint32_t s = 0; s < r; ++s)
+                if (s != g->rank && g->peer[s]) {
+                    mako_peer_close(g->ctx, g->peer[s]);
+                    g->peer[s] = nullptr;
+                }
+            return rc;
+        }
+    }
+    g->connected = true;
+    g->mapped = true;
+    g_error.clear();
+    return MAKO_OK;
+}
+
+int mako_group_connect_ptrs(mako_attn_group* g, void* const* areas)
+{
+    if (!g || !areas)
+        return fail(MAKO_EINVAL, "group_connect_ptrs: null argument");
+    if (g->connected)
+        return fail(MAKO_EINVAL, "group_connect_ptrs: already connected");
+    for (uint32_t r = 0; r < g->n_ranks; ++r)
+        if (r != g->rank && (!areas[r] || !aligned16(areas[r])))
+            return fail(MAKO_EINVAL, "group_connect_ptrs: area of rank %u null or unaligned", r);
+    for (uint32_t r = 0; r < g->n_ranks; ++r)
+        if (r != g->rank)
+            g->peer[r] = areas[r];
+    g->connected = true;
+    g_error.clear();
+    return MAKO_OK;
+}
+
+int mako_group_area(mako_attn_group* g, void** area, size_t* bytes)
+{
+    if (!g || !area || !bytes)
+        return fail(MAKO_EINVAL, "group_area: null argument");
+    *area = g->area;
+    *bytes = mako::xchg_bytes(g->rows_cap);
+    return MAKO_OK;
+}
+
+int mako_group_destroy(mako_attn_group* g)
+{
+    if (!g)
+        return MAKO_OK;
+    int rc = MAKO_OK;
+    {
+        DeviceGuard dg(g->ctx->device);
+        cudaDeviceSynchronize();  // no kernel of ours still signals through the mappings
+        for (uint32_t r = 0; r < g->n_ranks && g->mapped; ++r)
+            if (r != g->rank && g->peer[r]) {
+                cudaError_t e = cudaIpcCloseMemHandle(g->peer[r]);
+                if (e != cudaSuccess && rc == MAKO_OK)
+                    rc = cuda_fail("group_destroy: close", e);
+            }
+        if (g->area) {
+            cudaError_t e = cudaFree(g->area);
+            if (e != cudaSuccess && rc == MAKO_OK)
+                rc = cuda_fail("group_destroy: free", e);
+        }
+    }
+    delete g;
+    return rc;
+}
+
+int mako_attention_gather(mako_attn_group* g, void* stream, int dtype, const void* q, const void* k, const void* v,
+                          float* const* o_ranks, uint32_t n_q, uint32_t q_pad, uint32_t n_k, uint32_t k_pad,
+                          uint32_t heads, uint32_t kv_heads, uint32_t head0, uint32_t q_pos0, uint32_t block,
+                          uint32_t width)
+{
+    if (int rc = check_group(g, dtype))
+        return rc;
+    mako_attn_ctx* ctx = g->ctx;
+    if (ctx->cc_major != 10)
+        return fail(MAKO_ENOTSUP, "attention_gather: the tcgen05 kernel needs sm_100 (sm_%d)", ctx->cc_major * 10);
+    if (!heads || !kv_heads || heads % kv_heads)
+        return fail(MAKO_EINVAL, "attention_gather: %u heads over %u kv heads", heads, kv_heads);
+    if (q_pad % 64 || q_pad < n_q || k_pad < n_k)
+        return fail(MAKO_EINVAL, "attention_gather: q_pad %u (a multiple of 64, at least n_q %u), k_pad %u (at least "
+                                 "n_k %u)", q_pad, n_q, k_pad, n_k);
+    if (uint64_t(head0 + heads) * 128 > width)
+        return fail(MAKO_EINVAL, "attention_gather: heads [%u, %u) of 128 beyond o rows of %u floats", head0,
+                    head0 + heads, width);
+    if (!q || !k || !v || !o_ranks || !aligned16(q) || !aligned16(k) || !aligned16(v))
+        return fail(MAKO_EINVAL, "attention_gather: null or unaligned tensor (16-byte alignment)");
+    for (uint32_t r = 0; r < g->n_ranks; ++r)
+        if (!o_ranks[r] || !aligned16(o_ranks[r]))
+            return fail(MAKO_EINVAL, "attention_gather: o of rank %u null or unaligned", r);
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    auto st = static_cast<cudaStream_t>(stream);
+    mako::AttnParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = o_ranks[g->rank];
+    p.n_q = n_q;
+    p.q_pad = q_pad;
+    p.n_k = n_k;
+    p.k_pad = k_pad;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.q_pos0 = q_pos0;
+    p.block = block;
+    p.width = width;
+    p.scale = 1.0f / sqrtf(128.0f);
+    p.n_od = g->n_ranks;
+    p.head0 = head0;
+    for (uint32_t r = 0; r < g->n_ranks; ++r)  // own copy first: the local store is the cheap one
+        p.od[r] = o_ranks[(g->rank + r) % g->n_ranks];
+    void *v16 = nullptr, *vmax = nullptr, *vinv = nullptr;
+    if (dtype == MAKO_BF16) {
+        if (int rc = scratch(ctx, "v16", size_t(kv_heads) * k_pad * 128 * 2, &v16))
+            return rc;
+        if (int rc = scratch(ctx, "vmax", size_t(kv_heads) * 4, &vmax))
+            return rc;
+        if (int rc = scratch(ctx, "vinv", size_t(kv_heads) * 4, &vinv))
+            return rc;
+        cudaError_t e = mako::launch_v_to_f16(v, v16, static_cast<uint32_t*>(vmax), static_cast<float*>(vinv),
+                                              kv_heads, k_pad, n_k, nullptr, ctx->num_sms, st);
+        if (e != cudaSuccess)
+            return cuda_fail("attention_gather (V to fp16)", e);
+        ctx->launches += 2;
+    }
+    const mako::XchgParams x = xchg_params(g);
+    cudaError_t e = mako::launch_group_barrier(x, 0, st);
+    if (e != cudaSuccess)
+        return cuda_fail("attention_gather (enter barrier)", e);
+    if (n_q) {
+        KernelTimer t(ctx, st);
+        e = mako::launch_attn_tc(p, dtype, v16, static_cast<const float*>(vinv), ctx->err, st);
+        t.stop();
+        if (e != cudaSuccess)
+            return cuda_fail("attention_gather (tcgen05)", e);
+    }
+    ctx->launches += n_q ? 3 : 2;
+    return launched("attention_gather (done barrier)", mako::launch_group_barrier(x, 1, st));
+}
+
+int mako_attention_decode_kv_sharded(mako_attn_group* g, void* stream, int dtype, const void* q, const void* k,
+                                     const void* v, float* o, uint32_t batch, const int32_t* kv_len,
+                                     uint32_t max_kv_len, uint32_t heads, uint32_t kv_heads, uint32_t dim,
+                                     uint32_t k_stride)
+{
+    if (int rc = check_group(g, dtype))
+        return rc;
+    mako_attn_ctx* ctx = g->ctx;
+    if (dim != 64 && dim != 128 && dim != 256)
+        return fail(MAKO_EINVAL, "decode_kv_sharded: heads of %u", dim);
+    if (!heads || !kv_heads || heads % kv_heads)
+        return fail(MAKO_EINVAL, "decode_kv_sharded: %u heads over %u kv heads", heads, kv_heads);
+    if (max_kv_len > k_stride)
+        return fail(MAKO_EINVAL, "decode_kv_sharded: max_kv_len %u beyond the cache's %u rows", max_kv_len, k_stride);
+    if (uint64_t(batch) * heads > g->rows_cap)
+        return fail(MAKO_EINVAL, "decode_kv_sharded: %u sequences x %u heads beyond the group's %u rows", batch, heads,
+                    g->rows_cap);
+    if (!q || !k || !v || !o || !kv_len || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(MAKO_EINVAL, "decode_kv_sharded: null or unaligned tensor (16-byte alignment)");
+    if (batch == 0)
+        return MAKO_OK;
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    mako::DecodeParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = o;
+    p.kv_len = kv_len;
+    p.q_bstride = uint64_t(heads) * dim;
+    p.q_hstride = dim;
+    p.k_hstride = uint64_t(k_stride) * dim;
+    p.k_bstride = uint64_t(kv_heads) * p.k_hstride;
+    p.o_bstride = uint64_t(heads) * dim;
+    p.batch = batch;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.scale = 1.0f / sqrtf(float(dim));
+    p.keep_partials = 1;
+    mako::decode_plan(max_kv_len, batch, kv_heads, heads, ctx->num_sms, ctx->decode_chunk, &p.chunk, &p.n_splits);
+    void *op, *mlp;
+    if (int rc = scratch(ctx, "dec_o", size_t(batch) * heads * p.n_splits * dim * 4, &op))
+        return rc;
+    if (int rc = scratch(ctx, "dec_ml", size_t(batch) * heads * p.n_splits * 8, &mlp))
+        return rc;
+    p.o_part = static_cast<float*>(op);
+    p.ml_part = static_cast<float2*>(mlp);
+    auto st = static_cast<cudaStream_t>(stream);
+    KernelTimer t(ctx, st);
+    cudaError_t e = mako::launch_decode_split(p, dtype, int(dim), st);
+    t.stop();
+    if (e != cudaSuccess)
+        return cuda_fail("decode_kv_sharded (splits)", e);
+    ctx->launches += 2;
+    return launched("decode_kv_sharded (exchange)", mako::launch_decode_xchg(p, xchg_params(g), int(dim), st));
 }
 
 } // extern "C"

@@ -53,7 +53,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long lo
 
 // ---- TMA -----------------------------------------------------------------------------------------------------------
 
-// A 3-D tile of `map` at (c0, c1, c2) into shared memory, completing on `bar` (no multicast).
+// A 3-D tile of `map` at (c0, c1, c2) into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2)
 {
     asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"

@@ -13,15 +13,24 @@ LIB_PATH = os.path.join(HERE, "libmako_attn.so")
 
 F16, BF16 = 0, 1
 OK, EINVAL, ENOMEM, ECUDA, ENOTSUP = 0, -22, -12, -5, -95
-OPT_PREFILL_KERNEL, OPT_DECODE_ROUTE, OPT_DECODE_CHUNK = 1, 2, 3
+OPT_PREFILL_KERNEL, OPT_DECODE_ROUTE, OPT_DECODE_CHUNK, OPT_KERNEL_TIMING = 1, 2, 3, 4
 UINT32_MAX = 0xFFFFFFFF
 
 # Every symbol include/mako_attn.h declares, for the load check.
 SYMBOLS = (
     "mako_attn_last_error", "mako_attn_version", "mako_attn_create", "mako_attn_destroy", "mako_attn_set_option",
-    "mako_attn_launches", "mako_attn_device_error", "mako_attention", "mako_attention_decode", "mako_cube_select", "mako_attention_sparse",
+    "mako_attn_launches", "mako_attn_device_error", "mako_attn_kernel_times", "mako_attention", "mako_attention_decode", "mako_cube_select", "mako_attention_sparse",
     "mako_attention_block_sparse", "mako_attention_decode_noalloc",
+    "mako_peer_alloc", "mako_peer_free", "mako_peer_open", "mako_peer_close", "mako_group_create", "mako_group_connect",
+    "mako_group_destroy", "mako_attention_gather", "mako_attention_decode_kv_sharded", "mako_group_connect_ptrs",
+    "mako_group_area",
 )
+MAX_RANKS = 8
+
+
+class IpcHandle(ctypes.Structure):
+    """mako_ipc_handle: 64 opaque bytes a process passes to the others of its box."""
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 _lib = None
 
@@ -49,6 +58,7 @@ def lib():
     L.mako_attn_set_option.argtypes = [p, i32, i64]
     L.mako_attn_launches.argtypes = [p, ctypes.POINTER(ctypes.c_uint64)]
     L.mako_attn_device_error.argtypes = [p, ctypes.POINTER(ctypes.c_int)]
+    L.mako_attn_kernel_times.argtypes = [p, ctypes.POINTER(ctypes.c_float), u32, ctypes.POINTER(u32)]
     L.mako_attention.argtypes = [p, p, i32, p, p, p, p] + [u32] * 10
     L.mako_attention_decode.argtypes = [p, p, i32, p, p, p, p, u32, p, u32, u32, u32, u32, u32]
     L.mako_cube_select.argtypes = ([p, p, i32, p, p] + [u32] * 4 + [p, u32, ctypes.POINTER(p), ctypes.POINTER(p)]
@@ -56,6 +66,18 @@ def lib():
     L.mako_attention_sparse.argtypes = [p, p, i32, p, p, p, p] + [u32] * 11 + [p, p, p, p]
     L.mako_attention_block_sparse.argtypes = [p, p, i32, p, p, p, p, u32, u32, u32, p, p, u32]
     L.mako_attention_decode_noalloc.argtypes = [p, i32, p, p, p, p, u32, p, u32, u32, u32, u32, u32]
+    H = ctypes.POINTER(IpcHandle)
+    L.mako_peer_alloc.argtypes = [p, ctypes.c_size_t, ctypes.POINTER(p), H]
+    L.mako_peer_free.argtypes = [p, p]
+    L.mako_peer_open.argtypes = [p, H, ctypes.POINTER(p)]
+    L.mako_peer_close.argtypes = [p, p]
+    L.mako_group_create.argtypes = [p, u32, u32, u32, ctypes.POINTER(p), H]
+    L.mako_group_connect.argtypes = [p, H]
+    L.mako_group_destroy.argtypes = [p]
+    L.mako_group_connect_ptrs.argtypes = [p, ctypes.POINTER(p)]
+    L.mako_group_area.argtypes = [p, ctypes.POINTER(p), ctypes.POINTER(ctypes.c_size_t)]
+    L.mako_attention_gather.argtypes = [p, p, i32, p, p, p, ctypes.POINTER(p)] + [u32] * 10
+    L.mako_attention_decode_kv_sharded.argtypes = [p, p, i32, p, p, p, p, u32, p, u32, u32, u32, u32, u32]
     for name in SYMBOLS:
         if name != "mako_attn_last_error":
             getattr(L, name).restype = i32
@@ -137,6 +159,13 @@ class Context:
         _check(lib().mako_attn_device_error(self._h, ctypes.byref(n)))
         return n.value
 
+    def kernel_times(self, cap: int = 4096):
+        """Milliseconds of each main kernel recorded while OPT_KERNEL_TIMING was on (waits for them; then forgets)."""
+        buf = (ctypes.c_float * cap)()
+        n = ctypes.c_uint32()
+        _check(lib().mako_attn_kernel_times(self._h, buf, cap, ctypes.byref(n)))
+        return [buf[i] for i in range(min(n.value, cap))]
+
     def launches(self) -> int:
         n = ctypes.c_uint64()
         _check(lib().mako_attn_launches(self._h, ctypes.byref(n)))
@@ -176,3 +205,93 @@ class Context:
         _check(lib().mako_attention_block_sparse(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k), _ptr(v),
                                                  _ptr(o), n, heads, kv_heads, _ptr(lists), _ptr(counts),
                                                  lists.shape[-1]))
+
+
+# ---- multi-GPU (one process per GPU; handles travel through the caller's own channel) ------------------------------
+
+def _handle_bytes(h: IpcHandle) -> bytes:
+    return bytes(h.bytes)
+
+
+def _handle_from(b: bytes) -> IpcHandle:
+    h = IpcHandle()
+    ctypes.memmove(h.bytes, b, 64)
+    return h
+
+
+class PeerBuffer:
+    """A device buffer every rank maps (mako_peer_alloc here, mako_peer_open of the others' handles).
+
+    `exchange(handle_bytes) -> list of every rank's handle bytes, in rank order` is the caller's channel, e.g.
+    torch.distributed.all_gather_object.  `tensor` views this rank's buffer; `ptrs[r]` addresses rank r's."""
+
+    def __init__(self, ctx: "Context", nbytes: int, rank: int, exchange, shape=None, typestr="<f4"):
+        self._ctx = ctx
+        self._ptr = ctypes.c_void_p()
+        h = IpcHandle()
+        _check(lib().mako_peer_alloc(ctx._h, nbytes, ctypes.byref(self._ptr), ctypes.byref(h)))
+        handles = exchange(_handle_bytes(h))
+        self.ptrs = []
+        self._opened = []
+        for r, hb in enumerate(handles):
+            if r == rank:
+                self.ptrs.append(self._ptr.value)
+                continue
+            q = ctypes.c_void_p()
+            _check(lib().mako_peer_open(ctx._h, ctypes.byref(_handle_from(hb)), ctypes.byref(q)))
+            self._opened.append(q)
+            self.ptrs.append(q.value)
+        itemsize = int(typestr[2:])
+        self.tensor = device_view(self._ptr.value, shape or (nbytes // itemsize,), typestr)
+
+    def close(self):
+        for q in self._opened:
+            lib().mako_peer_close(self._ctx._h, q)
+        self._opened = []
+        if self._ptr:
+            lib().mako_peer_free(self._ctx._h, self._ptr)
+            self._ptr = ctypes.c_void_p()
+
+
+class Group:
+    """This rank's mako_attn_group: created, its handle exchanged through `exchange`, connected."""
+
+    def __init__(self, ctx: "Context", rank: int, n_ranks: int, max_rows: int, exchange=None):
+        """exchange None: connect later with connect_ptrs (ranks sharing this process)."""
+        self._ctx = ctx
+        self._h = ctypes.c_void_p()
+        h = IpcHandle()
+        _check(lib().mako_group_create(ctx._h, rank, n_ranks, max_rows, ctypes.byref(self._h), ctypes.byref(h)))
+        self.rank, self.n_ranks = rank, n_ranks
+        if exchange is not None:
+            handles = exchange(_handle_bytes(h))
+            arr = (IpcHandle * n_ranks)(*[_handle_from(b) for b in handles])
+            _check(lib().mako_group_connect(self._h, arr))
+
+    def area(self):
+        """(device pointer, bytes) of this rank's exchange area."""
+        a, n = ctypes.c_void_p(), ctypes.c_size_t()
+        _check(lib().mako_group_area(self._h, ctypes.byref(a), ctypes.byref(n)))
+        return a.value, n.value
+
+    def connect_ptrs(self, areas):
+        arr = (ctypes.c_void_p * self.n_ranks)(*areas)
+        _check(lib().mako_group_connect_ptrs(self._h, arr))
+
+    def close(self):
+        if self._h:
+            _check(lib().mako_group_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def attention_gather(self, q, k, v, o_ptrs, n_q, q_pad, n_k, k_pad, heads, kv_heads, head0, width, q_pos0=0,
+                         block=UINT32_MAX, stream=None):
+        arr = (ctypes.c_void_p * len(o_ptrs))(*o_ptrs)
+        _check(lib().mako_attention_gather(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k), _ptr(v), arr,
+                                           n_q, q_pad, n_k, k_pad, heads, kv_heads, head0, q_pos0, block & UINT32_MAX,
+                                           width))
+
+    def attention_decode_kv_sharded(self, q, k, v, o, kv_len, max_kv_len, heads, kv_heads, dim, k_stride,
+                                    stream=None):
+        _check(lib().mako_attention_decode_kv_sharded(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k),
+                                                      _ptr(v), _ptr(o), kv_len.numel(), _ptr(kv_len), max_kv_len,
+                                                      heads, kv_heads, dim, k_stride))

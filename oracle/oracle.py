@@ -163,3 +163,49 @@ def sparse_test_fixture():
     cnt = np.zeros(f["cubes"], np.uint32)
     lib().oracle_sparse_test_fixture(_p(q), _p(k), _p(v), _p(valid), _p(map_), _p(cnt))
     return dict(q=q, k=k, v=v, valid=valid, map=map_, cnt=cnt, **f)
+
+
+# ---- split-KV partials and their log-sum-exp merge (numpy float64; the KV-sharded decode's two halves) -----------
+
+def decode_partial(dtype, q, k, v, kv_len, heads, kv_heads, dim, k_stride, start=None):
+    """Per (sequence, head) over keys [start[b], start[b] + kv_len[b]) of the cache: (o, m, l) with
+    m = max of the scores in log2 units (q.k * fp32(1/sqrt(dim)) * log2(e)), l = sum 2^(s - m), o = sum 2^(s - m) v
+    (unnormalised); an empty range gives m = -inf, l = 0, o = 0.  The decode's softmax (tests/sparse_attn_test.cpp:
+    131-180) split into parts so that merge_partials recovers it."""
+    kv_len = np.asarray(kv_len, np.int64)
+    batch = kv_len.size
+    start = np.zeros(batch, np.int64) if start is None else np.asarray(start, np.int64)
+    qf = from_bits(np.asarray(q).reshape(batch, heads, dim), dtype).astype(np.float64)
+    kf = from_bits(np.asarray(k).reshape(batch, kv_heads, k_stride, dim), dtype)
+    vf = from_bits(np.asarray(v).reshape(batch, kv_heads, k_stride, dim), dtype)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim))) * np.log2(np.e)
+    group = heads // kv_heads
+    o = np.zeros((batch, heads, dim))
+    m = np.full((batch, heads), -np.inf)
+    l = np.zeros((batch, heads))
+    for b in range(batch):
+        s0, n = int(start[b]), int(kv_len[b])
+        if n <= 0:
+            continue
+        for h in range(heads):
+            kk = kf[b, h // group, s0:s0 + n].astype(np.float64)
+            vv = vf[b, h // group, s0:s0 + n].astype(np.float64)
+            s = kk @ qf[b, h] * scale
+            m[b, h] = s.max()
+            p = np.exp2(s - m[b, h])
+            l[b, h] = p.sum()
+            o[b, h] = p @ vv
+    return o, m, l
+
+
+def merge_partials(parts):
+    """Log-sum-exp merge of [(o, m, l), ...] into the normalised output [batch][heads * dim]."""
+    M = np.max(np.stack([m for _, m, _ in parts]), axis=0)
+    tot = np.zeros_like(M)
+    acc = np.zeros_like(parts[0][0])
+    for o, m, l in parts:
+        w = np.where(m == -np.inf, 0.0, np.exp2(np.where(m == -np.inf, 0.0, m - np.where(M == -np.inf, 0.0, M))))
+        tot += l * w
+        acc += o * w[..., None]
+    out = np.where(tot[..., None] > 0, acc / np.where(tot > 0, tot, 1.0)[..., None], 0.0)
+    return out.reshape(out.shape[0], -1).astype(np.float32)
