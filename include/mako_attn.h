@@ -126,7 +126,8 @@ int mako_cube_select(mako_attn_ctx* ctx, void* stream, int dtype, const void* q,
  * rows of [dense0, dense1); a later tile attends every valid key below n_k.  valid [k_pad] uint8; query row r's
  * output goes to o row map[r] (map [q_pad] int32, < 0: dropped).  Replaces TransformerRuntime::attention_sparse
  * (src/models/runtime.hpp:109-111, src/models/runtime.cpp:305-317): q_pad a multiple of 64, k_pad of 128, dense0
- * of 32; also dense0 <= dense1 <= k_pad, n_cubes * 64 <= q_pad and <= k_pad, width >= heads * 128. */
+ * of 32; also dense0 <= dense1 <= k_pad, n_cubes * 64 <= q_pad and <= k_pad, width >= heads * 128, valid 16-byte
+ * aligned like the tensors (the kernel reads it 16 keys at a time). */
 int mako_attention_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v,
                           float* o, uint32_t n_q, uint32_t q_pad, uint32_t n_k, uint32_t k_pad, uint32_t heads,
                           uint32_t kv_heads, uint32_t width, uint32_t n_cubes, uint32_t topk, uint32_t dense0,

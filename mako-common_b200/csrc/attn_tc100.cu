@@ -192,9 +192,9 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                 for (uint32_t x = 0; x < 2; ++x) {
                     const uint32_t j = pv_next[x];
                     if (j < nb && qk_next[x] > j) {
-                        if (v_ok == j && mbar_try_wait(v_full(j % TNS), (j / TNS) & 1))
+                        if (v_ok == j && mbar_test(v_full(j % TNS), (j / TNS) & 1))
                             v_ok = j + 1;
-                        if (v_ok > j && mbar_try_wait(p_full(x), j & 1)) {
+                        if (v_ok > j && mbar_test(p_full(x), j & 1)) {
                             fence_after();
                             pv(x, j % TNS, j > 0);
                             umma_commit(pv_done(x));
@@ -206,9 +206,9 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                     }
                     const uint32_t j1 = qk_next[x];
                     if (j1 < nb && pv_next[x] == j1) {
-                        if (k_ok == j1 && mbar_try_wait(k_full(j1 % TNS), (j1 / TNS) & 1))
+                        if (k_ok == j1 && mbar_test(k_full(j1 % TNS), (j1 / TNS) & 1))
                             k_ok = j1 + 1;
-                        if (k_ok > j1 && mbar_try_wait(pv_done(x), (j1 - 1) & 1)) {
+                        if (k_ok > j1 && mbar_test(pv_done(x), (j1 - 1) & 1)) {
                             fence_after();
                             qk(x, j1 % TNS);
                             umma_commit(s_full(x));

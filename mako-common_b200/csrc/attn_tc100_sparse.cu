@@ -10,32 +10,44 @@
 // partner's is padded with empty passes; an entry >= n_cubes is skipped.  Masking per key: valid[key] and the pass's
 // key range (ops.metal:1109); output row r goes to o row map[r], dropped when < 0 (ops.metal:1174-1184).
 //
-// CTA: two such tiles (A, B) with their own single-stage K and V buffers (the two tiles' loads and products
-// interleave), warp 0 TMA (K / V as 64-row boxes so each half can come from anywhere), warp 1 the UMMA issuer
-// (whichever product of either tile is ready), warps 4-7 / 8-11 the softmax of tile A / B, one row per thread.
-// TMEM as the dense kernel: S_A, S_B, O_A, O_B.  Precision, bounded waits and the error flag as the dense kernel.
+// One tile per CTA (384 threads): warp 0 issues the K loads and warp 2 the V loads (TMA, 64-row boxes so each half
+// can come from anywhere, into 3-stage rings), warp 1 issues UMMA, and warps 4-11 run the softmax and the epilogue:
+// each query row (TMEM lane) belongs to one thread of warps 4-7 and one of warps 8-11, which take half of the row's
+// columns each and agree on the row maximum through shared memory, so two warps per sub-partition share the exp unit.
+// TMEM (512 columns): S in two buffers (0-127, 128-255), O (256-383), Q (384-447, loaded once by the softmax threads,
+// the A operand of Q K^T so that product reads only K from shared memory) and P (448-511, fp16 pairs, the A operand
+// of P.V).  Q K^T of pass i + 2 waits only until the softmax has read S(i), so the tensor core runs Q K^T ahead while
+// the softmax works; the softmax writes P(i) once P.V(i - 1) has finished reading P(i - 1).  Precision, bounded waits
+// and the error flag as the dense kernel (attn_tc100.cu).
 #include "common.cuh"
 #include "kernels.h"
 #include "tc100.cuh"
 
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 namespace mako {
 namespace {
 
 using namespace tc;
 
-constexpr int SD = 128, SNT = 384;
-constexpr uint32_t QBOX = 128 * 64 * 2;  // a 128-row x 64-value box: 16 KB
-constexpr uint32_t HBOX = 64 * 64 * 2;   // a 64-row x 64-value box: 8 KB
-constexpr uint32_t STILE = 2 * QBOX;     // 128 rows x 128 values
-constexpr uint32_t S_Q = 0, S_K = 2 * STILE, S_V = 4 * STILE, S_BAR = 6 * STILE;
-constexpr uint32_t S_TOTAL = S_BAR + 256 + 1024;
+constexpr int SD = 128, SNT = 384, NST = 3;
+constexpr uint32_t DBOX = 128 * 64 * 2;  // one d-half of a 128-row tile: 16 KB
+constexpr uint32_t HBOX = 64 * 64 * 2;   // a 64-row x 64-value TMA box: 8 KB
+constexpr uint32_t STILE = 2 * DBOX;     // 128 rows x 128 values
+constexpr uint32_t S_K = 0, S_V = NST * STILE, S_BAR = 2 * NST * STILE;
+constexpr uint32_t S_XMAX = S_BAR + 256;   // float [2 passes][2 column halves][128 rows]: partial row maxima
+constexpr uint32_t S_LSUM = S_XMAX + 2048;  // float [2 column halves][128 rows]: partial row sums
+constexpr uint32_t kListCache = 1024;        // list entries per cube kept in shared memory
+constexpr uint32_t S_LIST = S_LSUM + 1024;  // uint32 [2 cubes][kListCache]
+constexpr uint32_t S_TOTAL = S_LIST + 2 * kListCache * 4 + 1024;
+constexpr uint32_t COL_O = 256, COL_Q = 384, COL_P = 448;
 constexpr long long S_WAIT_LIMIT = 1ll << 31;
 
 struct __align__(64) SpParams {
-    CUtensorMap tq;      // q, 128-row boxes
     CUtensorMap tk, tv;  // k and v (or the fp16 copy of v), 64-row boxes
+    const void* q;
     float* o;
     int* err;
     const float* vinv;
@@ -56,7 +68,8 @@ struct TileInfo {
 
 __device__ __forceinline__ uint32_t list_entry(const SpParams& p, const void* base, uint64_t i)
 {
-    return p.sel_i32 ? uint32_t(static_cast<const int32_t*>(base)[i]) : uint32_t(static_cast<const uint16_t*>(base)[i]);
+    return p.sel_i32 ? uint32_t(__ldg(static_cast<const int32_t*>(base) + i))
+                     : uint32_t(__ldg(static_cast<const uint16_t*>(base) + i));
 }
 
 __device__ __forceinline__ TileInfo tile_info(const SpParams& p, uint32_t u, uint32_t h)
@@ -88,23 +101,26 @@ __device__ __forceinline__ TileInfo tile_info(const SpParams& p, uint32_t u, uin
     return t;
 }
 
-// Key rows of pass `pi`, half `hh` (tile rows 64 hh .. 64 hh + 63 of K / V): they start at j0; keys j < hi are in
-// range.  Cube passes: the half belongs to one query cube (empty: hi = j0 = 0).  Other passes: 128 consecutive keys.
-__device__ __forceinline__ void pass_keys(const SpParams& p, const TileInfo& t, uint32_t h, uint32_t pi, uint32_t hh,
-                                          uint32_t& j0, uint32_t& hi)
+// The list entry a cube pass reads (pass pi, half hh), or 0xFFFFFFFF when the list has no entry there; read well
+// before use so its latency hides behind a pass.
+__device__ __forceinline__ uint32_t raw_entry(const SpParams& p, const TileInfo& t, uint32_t h, uint32_t pi,
+                                              uint32_t hh)
+{
+    if (!(t.cube && pi < t.ns[hh]))
+        return 0xFFFFFFFFu;
+    return list_entry(p, p.sel, (uint64_t(h) * p.n_cubes + t.cube_id[hh]) * p.max_sel + pi);
+}
+// Key rows of pass `pi`, half `hh` (tile rows 64 hh .. 64 hh + 63 of K / V) start at j0; keys j < hi are in range.
+// Cube passes: the half belongs to one query cube, whose list entry for the pass is `raw` (none, or >= n_cubes: the
+// half is empty, hi = j0 = 0, and rows 0 .. 63 are still loaded so that the masked half of K / V holds finite
+// values).  Other passes: 128 consecutive keys of the dense rows or of all keys.
+__device__ __forceinline__ void keys_of(const SpParams& p, const TileInfo& t, uint32_t pi, uint32_t hh, uint32_t raw,
+                                        uint32_t& j0, uint32_t& hi)
 {
     if (t.cube && pi < t.ncp) {
-        if (pi < t.ns[hh]) {
-            const uint32_t c =
-                list_entry(p, p.sel, (uint64_t(h) * p.n_cubes + t.cube_id[hh]) * p.max_sel + pi);
-            if (c < p.n_cubes) {
-                j0 = c * 64;
-                hi = j0 + 64;
-                return;
-            }
-        }
-        j0 = 0;
-        hi = 0;
+        const bool ok = raw < p.n_cubes;
+        j0 = ok ? raw * 64 : 0;
+        hi = ok ? j0 + 64 : 0;
         return;
     }
     const uint32_t base = t.cube ? p.dense0 + (pi - t.ncp) * 128 : pi * 128;
@@ -118,39 +134,64 @@ __device__ __forceinline__ uint32_t pack_half2s(float lo, float hi)
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Masks (to -inf bits) the columns c of r whose key j0 + c is out of range or invalid.  NC columns from j0, which
+// is a multiple of 32 (cube starts, dense0 and 128-key steps), so valid[] is read 16 bytes at a time.
+template <int NC>
+__device__ __forceinline__ void mask_keys(uint32_t (&r)[NC], const uint8_t* valid, uint32_t j0, uint32_t hi)
+{
+    if (hi >= j0 + NC && !valid)
+        return;
+#pragma unroll
+    for (int c0 = 0; c0 < NC; c0 += 16) {
+        uint4 w = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
+        if (valid && j0 + c0 < hi)
+            w = __ldg(reinterpret_cast<const uint4*>(valid + j0 + c0));
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            const bool ok = j0 + c0 + c < hi && ((words[c >> 2] >> (8 * (c & 3))) & 0xFFu) != 0;
+            if (!ok)
+                r[c0 + c] = 0xFF800000u;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_constant__ SpParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* const gbase = smem_raw + (base - raw);
     const uint32_t sB = base + S_BAR;
-    const uint32_t q_full = sB;
-    auto k_full = [&](uint32_t x) { return sB + 8 + 8 * x; };
-    auto k_empty = [&](uint32_t x) { return sB + 24 + 8 * x; };
-    auto v_full = [&](uint32_t x) { return sB + 40 + 8 * x; };
-    auto v_empty = [&](uint32_t x) { return sB + 56 + 8 * x; };
-    auto s_full = [&](uint32_t x) { return sB + 72 + 8 * x; };
-    auto p_full = [&](uint32_t x) { return sB + 88 + 8 * x; };
-    auto pv_done = [&](uint32_t x) { return sB + 104 + 8 * x; };
-    const uint32_t mma_done = sB + 120, tmem_slot = sB + 128;
+    auto k_full = [&](uint32_t s) { return sB + 8 * s; };
+    auto k_empty = [&](uint32_t s) { return sB + 24 + 8 * s; };
+    auto v_full = [&](uint32_t s) { return sB + 48 + 8 * s; };
+    auto v_empty = [&](uint32_t s) { return sB + 72 + 8 * s; };
+    auto s_full = [&](uint32_t b) { return sB + 96 + 8 * b; };
+    auto s_free = [&](uint32_t b) { return sB + 112 + 8 * b; };
+    const uint32_t p_full = sB + 128, pv_done = sB + 136, q_ready = sB + 144, mma_done = sB + 152;
+    const uint32_t tmem_slot = sB + 160;
     volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t h = blockIdx.y, kvh = h / (p.heads / p.kv_heads);
-    const uint32_t pair = gridDim.x - 1 - blockIdx.x;  // the row tiles after the cubes (all keys) first
-    TileInfo ti[2] = {tile_info(p, 2 * pair, h), tile_info(p, 2 * pair + 1, h)};
+    const uint32_t u = gridDim.x - 1 - blockIdx.x;  // the row tiles after the cubes (all keys) first
+    const TileInfo t = tile_info(p, u, h);
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        for (uint32_t x = 0; x < 2; ++x) {
-            mbar_init(k_full(x), 1);
-            mbar_init(k_empty(x), 1);
-            mbar_init(v_full(x), 1);
-            mbar_init(v_empty(x), 1);
-            mbar_init(s_full(x), 1);
-            mbar_init(p_full(x), 128);
-            mbar_init(pv_done(x), 1);
+        for (uint32_t s = 0; s < NST; ++s) {
+            mbar_init(k_full(s), 1);
+            mbar_init(k_empty(s), 1);
+            mbar_init(v_full(s), 1);
+            mbar_init(v_empty(s), 1);
         }
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(s_full(b), 1);
+            mbar_init(s_free(b), 256);
+        }
+        mbar_init(p_full, 256);
+        mbar_init(pv_done, 1);
+        mbar_init(q_ready, 256);
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
@@ -163,181 +204,174 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     fence_after();
     const uint32_t tmem = *tmem_slot_ptr;
 
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            tma_prefetch_desc(&p.tq);
-            tma_prefetch_desc(&p.tk);
-            tma_prefetch_desc(&p.tv);
-            const uint32_t nq = ti[0].active + ti[1].active;
-            mbar_expect_tx(q_full, nq * STILE);
-            for (uint32_t x = 0; x < 2; ++x)
-                if (ti[x].active)
-                    for (int dh = 0; dh < 2; ++dh)
-                        tma_load_3d(base + S_Q + x * STILE + dh * QBOX, &p.tq, q_full, dh * 64, ti[x].row0, h);
-            uint32_t kn[2] = {0, 0}, vn[2] = {0, 0};
+    if ((warp == 0 || warp == 2) && lane == 0) {
+        // ---------------- TMA producers: warp 0 the K ring, warp 2 the V ring ----------------
+        if (t.np > 0) {
+            const bool is_k = warp == 0;
+            const CUtensorMap* map = is_k ? &p.tk : &p.tv;
+            const uint32_t ring = base + (is_k ? S_K : S_V);
+            tma_prefetch_desc(map);
             bool ok = true;
-            long long idle_since = clock64();
-            auto load = [&](const CUtensorMap* map, uint32_t dst, uint32_t bar, uint32_t x, uint32_t pi) {
-                mbar_expect_tx(bar, STILE);
-                for (uint32_t hh = 0; hh < 2; ++hh) {
-                    uint32_t j0, hi;
-                    pass_keys(p, ti[x], h, pi, hh, j0, hi);
-                    for (int dh = 0; dh < 2; ++dh)
-                        tma_load_3d(dst + dh * QBOX + hh * HBOX, map, bar, dh * 64, int(j0), kvh);
+            uint32_t issued = 0;
+            uint32_t rawn[2] = {raw_entry(p, t, h, 0, 0), raw_entry(p, t, h, 0, 1)};
+            for (uint32_t i = 0; i < t.np; ++i) {
+                uint32_t j0[2], hi;
+                keys_of(p, t, i, 0, rawn[0], j0[0], hi);
+                keys_of(p, t, i, 1, rawn[1], j0[1], hi);
+                if (i + 1 < t.np) {  // the next pass's list entries are read while this pass waits for its stage
+                    rawn[0] = raw_entry(p, t, h, i + 1, 0);
+                    rawn[1] = raw_entry(p, t, h, i + 1, 1);
                 }
-            };
-            while (ok && (kn[0] < ti[0].np || vn[0] < ti[0].np || kn[1] < ti[1].np || vn[1] < ti[1].np)) {
-                bool progressed = false;
-                for (uint32_t x = 0; x < 2; ++x) {
-                    if (kn[x] < ti[x].np && (kn[x] == 0 || mbar_try_wait(k_empty(x), (kn[x] - 1) & 1))) {
-                        load(&p.tk, base + S_K + x * STILE, k_full(x), x, kn[x]);
-                        ++kn[x];
-                        progressed = true;
-                    }
-                    if (vn[x] < ti[x].np && (vn[x] == 0 || mbar_try_wait(v_empty(x), (vn[x] - 1) & 1))) {
-                        load(&p.tv, base + S_V + x * STILE, v_full(x), x, vn[x]);
-                        ++vn[x];
-                        progressed = true;
-                    }
-                }
-                if (progressed)
-                    idle_since = clock64();
-                else if (clock64() - idle_since > S_WAIT_LIMIT)
+                const uint32_t s = i % NST, ph = (i / NST) & 1;
+                if (i >= NST && !mbar_wait(is_k ? k_empty(s) : v_empty(s), ph ^ 1, S_WAIT_LIMIT)) {
                     ok = false;
+                    break;
+                }
+                const uint32_t full = is_k ? k_full(s) : v_full(s);
+                mbar_expect_tx(full, STILE);
+                for (uint32_t hh = 0; hh < 2; ++hh)
+                    for (int dh = 0; dh < 2; ++dh)
+                        tma_load_3d(ring + s * STILE + dh * DBOX + hh * HBOX, map, full, dh * 64, int(j0[hh]), kvh);
+                ++issued;
             }
             if (!ok)
                 atomicExch(p.err, 11);
             // Our copies in flight land before the CTA leaves (already so on the normal path).
-            mbar_wait(q_full, 0, S_WAIT_LIMIT);
-            for (uint32_t x = 0; x < 2; ++x) {
-                if (kn[x])
-                    mbar_wait(k_full(x), (kn[x] - 1) & 1, S_WAIT_LIMIT);
-                if (vn[x])
-                    mbar_wait(v_full(x), (vn[x] - 1) & 1, S_WAIT_LIMIT);
-            }
+            for (uint32_t i = issued > NST ? issued - NST : 0; i < issued; ++i)
+                mbar_wait(is_k ? k_full(i % NST) : v_full(i % NST), (i / NST) & 1, S_WAIT_LIMIT);
         }
     } else if (warp == 1) {
         // ---------------- UMMA issuer ----------------
-        if (lane == 0 && (ti[0].np || ti[1].np)) {
+        // Fixed order QK(0), QK(1), then per pass PV(i), QK(i + 2): QK(i + 2) needs only the softmax to have read
+        // S(i), which it did before writing P(i), so both products of a pass go to the tensor core back to back.
+        // Each group is followed by one commit (s_full / pv_done); the K and V stages are released by a softmax
+        // thread that observes those completions anyway.
+        if (lane == 0 && t.np > 0) {
             const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, 128, 128);
             const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, 128, SD);
-            auto qk = [&](uint32_t x) {
+            auto qk = [&](uint32_t j) {
+                const uint32_t s = j % NST, b = j & 1;
+                bool w = mbar_wait(k_full(s), (j / NST) & 1, S_WAIT_LIMIT);
+                if (w && j >= 2)
+                    w = mbar_wait(s_free(b), ((j - 2) >> 1) & 1, S_WAIT_LIMIT);
+                if (!w)
+                    return false;
+                fence_after();
 #pragma unroll
-                for (uint32_t ks = 0; ks < SD / 16; ++ks) {
-                    const uint32_t off = (ks >> 2) * QBOX + (ks & 3) * 32;
-                    umma_ss(tmem + x * 128, sdesc(base + S_Q + x * STILE + off, 16, 1024),
-                            sdesc(base + S_K + x * STILE + off, 16, 1024), idesc_qk, ks > 0);
-                }
+                for (uint32_t ks = 0; ks < SD / 16; ++ks)
+                    umma_ts(tmem + b * 128, tmem + COL_Q + ks * 8,
+                            sdesc(base + S_K + s * STILE + (ks >> 2) * DBOX + (ks & 3) * 32, 16, 1024), idesc_qk,
+                            ks > 0);
+                umma_commit(s_full(b));
+                return true;
             };
-            auto pv = [&](uint32_t x, bool acc) {
+            bool ok = mbar_wait(q_ready, 0, S_WAIT_LIMIT);
+            fence_after();
+            ok = ok && qk(0) && (t.np < 2 || qk(1));
+            for (uint32_t i = 0; ok && i < t.np; ++i) {
+                const uint32_t s = i % NST;
+                ok = mbar_wait(p_full, i & 1, S_WAIT_LIMIT) && mbar_wait(v_full(s), (i / NST) & 1, S_WAIT_LIMIT);
+                if (!ok)
+                    break;
+                fence_after();
 #pragma unroll
                 for (uint32_t kk = 0; kk < 8; ++kk)
-                    umma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
-                            sdesc(base + S_V + x * STILE + kk * 2048, QBOX, 1024), idesc_pv, acc || kk > 0);
-            };
-            bool ok = mbar_wait(q_full, 0, S_WAIT_LIMIT);
-            uint32_t qn[2] = {0, 0}, pn[2] = {0, 0};
-            long long idle_since = clock64();
-            while (ok && (pn[0] < ti[0].np || pn[1] < ti[1].np)) {
-                bool progressed = false;
-#pragma unroll
-                for (uint32_t x = 0; x < 2; ++x) {
-                    const uint32_t i = qn[x];
-                    // QK_X(i): K_X(i) landed and PV_X(i-1) finished (it read the P this overwrites)
-                    if (i < ti[x].np && pn[x] == i && mbar_try_wait(k_full(x), i & 1) &&
-                        (i == 0 || mbar_try_wait(pv_done(x), (i - 1) & 1))) {
-                        fence_after();
-                        qk(x);
-                        umma_commit(s_full(x));
-                        umma_commit(k_empty(x));
-                        qn[x] = i + 1;
-                        progressed = true;
-                    }
-                    const uint32_t j = pn[x];
-                    // PV_X(j): P_X(j) written and V_X(j) landed
-                    if (j < qn[x] && mbar_try_wait(p_full(x), j & 1) && mbar_try_wait(v_full(x), j & 1)) {
-                        fence_after();
-                        pv(x, j > 0);
-                        umma_commit(pv_done(x));
-                        umma_commit(v_empty(x));
-                        pn[x] = j + 1;
-                        progressed = true;
-                    }
-                }
-                if (progressed)
-                    idle_since = clock64();
-                else if (clock64() - idle_since > S_WAIT_LIMIT)
-                    ok = false;
+                    umma_ts(tmem + COL_O, tmem + COL_P + kk * 8, sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024),
+                            idesc_pv, i > 0 || kk > 0);
+                umma_commit(pv_done);
+                if (i + 2 < t.np)
+                    ok = qk(i + 2);
             }
             if (!ok)
                 atomicExch(p.err, 12);
-            umma_commit(mma_done);
+            umma_commit(mma_done);  // every MMA issued above has finished before TMEM is freed
             mbar_wait(mma_done, 0, S_WAIT_LIMIT);
         }
     } else if (warp >= 4) {
-        // ---------------- softmax (and epilogue) of tile X ----------------
-        const uint32_t x = (warp - 4) >> 2, ql = (warp & 3) * 32, row = ql + lane, hr = ql >> 6;
-        const TileInfo& t = ti[x];
-        const uint32_t tl = tmem + (ql << 16);
-        const uint32_t colS = x * 128, colO = 256 + x * 128;
+        // ---------------- softmax and epilogue: tile row `row`, column half `c` ----------------
+        const uint32_t c = (warp - 4) >> 2, qd = warp & 3, row = qd * 32 + lane, hr = row >> 6;
+        const uint32_t tl = tmem + ((qd * 32) << 16);
+        float* const xmax = reinterpret_cast<float*>(gbase + S_XMAX);
+        float* const lsum = reinterpret_cast<float*>(gbase + S_LSUM);
         const float scale = p.scale_log2;
         const uint64_t scale2 = pack2(scale, scale);
-        float m = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (uint32_t i = 0; i < t.np; ++i) {
-            ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), i & 1, S_WAIT_LIMIT));
-            if (!ok)
-                break;
-            fence_after();
-            const bool half = t.cube && i < t.ncp;  // this row sees only its cube's 64 keys
-            uint32_t r[4][32];
-            uint32_t j0, hi;
-            if (half) {
-                pass_keys(p, t, h, i, hr, j0, hi);
-                tmem_ld32(tl + colS + 64 * hr, r[0]);
-                tmem_ld32(tl + colS + 64 * hr + 32, r[1]);
-                tmem_wait_ld();
-                reg_fence(r[0]);
-                reg_fence(r[1]);
-                if (hi < j0 + 64 || p.valid) {
+        {
+            // half c of this row of Q: 64 16-bit values = 32 TMEM columns (zeros past q_pad)
+            const uint32_t grow = t.row0 + row;
+            uint32_t qr[32];
+            if (t.active && grow < p.q_pad) {
+                const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) +
+                                                                  (uint64_t(h) * p.q_pad + grow) * SD + 64 * c);
 #pragma unroll
-                    for (int c = 0; c < 64; ++c) {
-                        const uint32_t jj = j0 + c;
-                        if (jj >= hi || (p.valid && !p.valid[jj]))
-                            r[c >> 5][c & 31] = 0xFF800000u;
-                    }
+                for (int k = 0; k < 8; ++k) {
+                    const uint4 w = __ldg(src + k);
+                    qr[4 * k + 0] = w.x;
+                    qr[4 * k + 1] = w.y;
+                    qr[4 * k + 2] = w.z;
+                    qr[4 * k + 3] = w.w;
                 }
             } else {
-                pass_keys(p, t, h, i, 0, j0, hi);
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    tmem_ld32(tl + colS + c * 32, r[c]);
-                tmem_wait_ld();
+                for (int k = 0; k < 32; ++k)
+                    qr[k] = 0u;
+            }
+            tmem_st32(tl + COL_Q + 32 * c, qr);
+            tmem_wait_st();
+            fence_before();
+            mbar_arrive(q_ready);
+        }
+        // this row's cube list, copied to shared memory once (the loop reads it without global-load latency)
+        uint32_t* const lcache = reinterpret_cast<uint32_t*>(gbase + S_LIST);
+        const bool cached = t.cube && t.ncp <= kListCache;
+        if (cached)
+            for (uint32_t k = threadIdx.x - 128; k < 2 * kListCache; k += 256) {
+                const uint32_t hh = k / kListCache, pi = k % kListCache;
+                if (pi < t.ncp)
+                    lcache[k] = raw_entry(p, t, h, pi, hh);
+            }
+        named_bar(5, 256);
+        float m = -INFINITY, l = 0.0f;
+
+        // One pass over this thread's columns of S in NCH chunks of 32 (1: half of a cube pass's 64 keys; 2: half of
+        // 128 keys, the first chunk read again from TMEM for its exponentials so that only 32 scores are live).
+        // After a failed wait the thread skips the work but keeps meeting its partner at the named barrier (which
+        // cannot time out), so both column halves run the same number of passes.
+        auto pass = [&](auto nch_tag, uint32_t i, uint32_t key0, uint32_t hi) {
+            constexpr int NCH = decltype(nch_tag)::value;
+            const uint32_t b = i & 1;
+            // S columns of chunk k and the packed P columns it fills
+            auto s_col = [&](int k) { return NCH == 1 ? b * 128 + 64 * hr + 32 * c : b * 128 + 64 * c + 32 * k; };
+            auto p_col = [&](int k) { return NCH == 1 ? COL_P + 32 * hr + 16 * c : COL_P + 32 * c + 16 * k; };
+            uint32_t r[32];
+            float pmax = -INFINITY;
+            if (ok) {
+                fence_after();
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    reg_fence(r[c]);
-                if (hi < j0 + 128 || p.valid) {
-#pragma unroll
-                    for (int c = 0; c < 128; ++c) {
-                        const uint32_t jj = j0 + c;
-                        if (jj >= hi || (p.valid && !p.valid[jj]))
-                            r[c >> 5][c & 31] = 0xFF800000u;
+                for (int k = 0; k < NCH; ++k) {
+                    tmem_ld32(tl + s_col(k), r);
+                    tmem_wait_ld();
+                    reg_fence(r);
+                    if (NCH == 1) {
+                        fence_before();
+                        mbar_arrive(s_free(b));  // Q K^T(i + 2) may overwrite this buffer now
                     }
+                    mask_keys<32>(r, p.valid, key0 + 32 * k, hi);
+                    float mq[4] = {pmax, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                    for (int cc = 0; cc < 32; cc += 8)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            mq[e] = max3f(mq[e], __uint_as_float(r[cc + 2 * e]), __uint_as_float(r[cc + 2 * e + 1]));
+                    pmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
                 }
             }
-            const int ncol = half ? 64 : 128;
-            float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int c = 0; c < 128; c += 8) {
-                if (c < ncol) {
-#pragma unroll
-                    for (int s = 0; s < 4; ++s)
-                        mq[s] = max3f(mq[s], __uint_as_float(r[(c + 2 * s) >> 5][(c + 2 * s) & 31]),
-                                      __uint_as_float(r[(c + 2 * s + 1) >> 5][(c + 2 * s + 1) & 31]));
-                }
-            }
-            const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
+            // the row maximum over both column halves (partner: the same row in the other warpgroup)
+            xmax[(b * 2 + c) * 128 + row] = pmax;
+            named_bar(1 + qd, 64);
+            if (!ok)
+                return;
+            const float mx = fmaxf(pmax, xmax[(b * 2 + (c ^ 1)) * 128 + row]) * scale;
             float f = 1.0f;
             bool resc = false;
             if (mx > m + 8.0f) {
@@ -348,66 +382,92 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             }
             const float mneg = m == -INFINITY ? 0.0f : -m;
             const uint64_t mneg2 = pack2(mneg, mneg);
-            uint32_t pk[2][32];
-            uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
+            // P of the 32 scores in r as fp16 pairs, in place: pair cc into r[cc]
+            auto exps = [&]() {
+                uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                if (2 * c < ncol) {
-                    const uint64_t xv = pack2(__uint_as_float(r[(2 * c) >> 5][(2 * c) & 31]),
-                                              __uint_as_float(r[(2 * c + 1) >> 5][(2 * c + 1) & 31]));
-                    float a, b;
-                    unpack2(ffma2(xv, scale2, mneg2), a, b);
+                for (int cc = 0; cc < 16; ++cc) {
+                    float a, bb;
+                    unpack2(ffma2(pack2(__uint_as_float(r[2 * cc]), __uint_as_float(r[2 * cc + 1])), scale2, mneg2), a,
+                            bb);
                     a = ex2(a);
-                    b = ex2(b);
-                    sum2[c & 1] = fadd2(sum2[c & 1], pack2(a, b));
-                    pk[c >> 5][c & 31] = pack_half2s(a, b);
-                } else {
-                    pk[c >> 5][c & 31] = 0u;
+                    bb = ex2(bb);
+                    sum2[cc & 1] = fadd2(sum2[cc & 1], pack2(a, bb));
+                    r[cc] = pack_half2s(a, bb);
                 }
-            }
-            {
                 float s0, s1, s2, s3;
                 unpack2(sum2[0], s0, s1);
                 unpack2(sum2[1], s2, s3);
                 l += (s0 + s1) + (s2 + s3);
-            }
-            if (half) {
-                // P of this row's cube sits at packed columns 32 hr .. 32 hr + 31, zeros in the other cube's half
-                if (hr == 0) {
-                    tmem_st32(tl + colS, pk[0]);
-                    tmem_st32(tl + colS + 32, pk[1]);
-                } else {
-                    tmem_st32(tl + colS, pk[1]);
-                    tmem_st32(tl + colS + 32, pk[0]);
+            };
+            exps();  // the chunk still in registers (the last one read)
+            // P.V(i - 1) must have finished: it reads the P columns written below and adds to the O rescaled below.
+            if (i > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, S_WAIT_LIMIT));
+                if (!ok)
+                    return;
+                fence_after();
+                if (threadIdx.x == 128)
+                    mbar_arrive(v_empty((i - 1) % NST));  // PV(i - 1) has finished reading V(i - 1)
+                if (__any_sync(0xffffffffu, resc)) {
+                    const float g = resc ? f : 1.0f;
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        uint32_t o[32];
+                        tmem_ld32(tl + COL_O + 64 * c + 32 * k, o);
+                        tmem_wait_ld();
+                        reg_fence(o);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * g);
+                        tmem_st32(tl + COL_O + 64 * c + 32 * k, o);
+                    }
                 }
+            }
+            tmem_st16(tl + p_col(NCH - 1), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+            if (NCH == 1) {
+                // the other cube's packed columns of this row are zeros
+                tmem_st16_zero(tl + COL_P + 32 * (hr ^ 1) + 16 * c);
             } else {
-                tmem_st32(tl + colS, pk[0]);
-                tmem_st32(tl + colS + 32, pk[1]);
-            }
-            if (__any_sync(0xffffffffu, resc && i > 0)) {
-                const float g = resc ? f : 1.0f;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32(tl + colO + c * 32, o);
-                    tmem_wait_ld();
-                    reg_fence(o);
-#pragma unroll
-                    for (int k = 0; k < 32; ++k)
-                        o[k] = __float_as_uint(__uint_as_float(o[k]) * g);
-                    tmem_st32(tl + colO + c * 32, o);
-                }
+                tmem_ld32(tl + s_col(0), r);
+                tmem_wait_ld();
+                reg_fence(r);
+                fence_before();
+                mbar_arrive(s_free(b));
+                mask_keys<32>(r, p.valid, key0, hi);
+                exps();
+                tmem_st16(tl + p_col(0), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
             }
             tmem_wait_st();
             fence_before();
-            mbar_arrive(p_full(x));
+            mbar_arrive(p_full);
+        };
+
+        for (uint32_t i = 0; i < t.np; ++i) {
+            const bool half = t.cube && i < t.ncp;  // this row sees only its cube's 64 keys
+            uint32_t j0, hi;
+            const uint32_t hh = half ? hr : 0;
+            keys_of(p, t, i, hh, half ? (cached ? lcache[hh * kListCache + i] : raw_entry(p, t, h, i, hh)) : 0u, j0,
+                    hi);
+            if (ok)
+                ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, S_WAIT_LIMIT));
+            if (ok && threadIdx.x == 128)
+                mbar_arrive(k_empty(i % NST));  // QK(i) has finished reading K(i)
+            if (half)
+                pass(std::integral_constant<int, 1>{}, i, j0 + 32 * c, hi);
+            else
+                pass(std::integral_constant<int, 2>{}, i, j0 + 64 * c, hi);
         }
         if (ok && t.np > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(pv_done(x), (t.np - 1) & 1, S_WAIT_LIMIT));
+            ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (t.np - 1) & 1, S_WAIT_LIMIT));
             fence_after();
         }
         if (!ok && lane == 0)
             atomicExch(p.err, 13);
+        // the row sum over both halves
+        lsum[c * 128 + row] = l;
+        named_bar(1 + qd, 64);
+        l = lsum[row] + lsum[128 + row];
         // Store: rows below n_q that belong to this tile (a cube tile's half past the last cube is another tile's).
         const uint32_t grow = t.row0 + row;
         bool store = t.active && grow < p.n_q && (!t.cube || t.cube_id[hr] < p.n_cubes);
@@ -417,25 +477,25 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             store = dst >= 0;
         }
         const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
-        float* orow = p.o + uint64_t(dst) * p.width + uint64_t(h) * SD;
+        float* orow = p.o + uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * c;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int k = 0; k < 2; ++k) {
             uint32_t o[32];
             if (ok && t.np > 0) {
-                tmem_ld32(tl + colO + c * 32, o);
+                tmem_ld32(tl + COL_O + 64 * c + 32 * k, o);
                 tmem_wait_ld();
                 reg_fence(o);
             } else {
 #pragma unroll
-                for (int k = 0; k < 32; ++k)
-                    o[k] = 0u;
+                for (int e = 0; e < 32; ++e)
+                    o[e] = 0u;
             }
             if (store) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    *reinterpret_cast<float4*>(orow + c * 32 + k * 4) =
-                        make_float4(__uint_as_float(o[4 * k]) * inv, __uint_as_float(o[4 * k + 1]) * inv,
-                                    __uint_as_float(o[4 * k + 2]) * inv, __uint_as_float(o[4 * k + 3]) * inv);
+                for (int e = 0; e < 8; ++e)
+                    *reinterpret_cast<float4*>(orow + 32 * k + e * 4) =
+                        make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
+                                    __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
             }
         }
     }
@@ -485,9 +545,10 @@ cudaError_t launch_attn_tc_sparse(const AttnParams& a, int dtype, bool sel_i32, 
         return cudaSuccess;
     SpParams p;
     const bool bf = dtype == kBF16;
-    if (!map_rows(&p.tq, a.q, bf, a.q_pad, a.heads, 128) || !map_rows(&p.tk, a.k, bf, a.k_pad, a.kv_heads, 64) ||
-        !map_rows(&p.tv, bf ? v16 : a.v, false, a.k_pad, a.kv_heads, 64))
+    if (!map_rows(&p.tk, a.k, bf, a.k_pad, a.kv_heads, 64) || !map_rows(&p.tv, bf ? v16 : a.v, false, a.k_pad,
+                                                                         a.kv_heads, 64))
         return cudaErrorInvalidValue;
+    p.q = a.q;
     p.o = a.o;
     p.err = err;
     p.vinv = bf ? vinv : nullptr;
@@ -515,10 +576,9 @@ cudaError_t launch_attn_tc_sparse(const AttnParams& a, int dtype, bool sel_i32, 
     cudaError_t e = cudaFuncSetAttribute(attn_tc_sparse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_TOTAL);
     if (e != cudaSuccess)
         return e;
-    const uint32_t pairs = (p.tiles_total + 1) / 2;
-    if (pairs == 0)
+    if (p.tiles_total == 0)
         return cudaSuccess;
-    attn_tc_sparse_kernel<<<dim3(pairs, a.heads), SNT, S_TOTAL, st>>>(p);
+    attn_tc_sparse_kernel<<<dim3(p.tiles_total, a.heads), SNT, S_TOTAL, st>>>(p);
     return cudaGetLastError();
 }
 

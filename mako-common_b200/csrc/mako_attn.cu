@@ -565,7 +565,7 @@ int mako_attention_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const voi
         return fail(MAKO_EINVAL, "attention_sparse: rows n_q %u q_pad %u n_k %u k_pad %u dense [%u, %u) cubes %u width %u",
                     n_q, q_pad, n_k, k_pad, dense0, dense1, n_cubes, width);
     if (!q || !k || !v || !o || !valid || !map || (n_cubes && (!sel || !nsel)) || !aligned16(q) || !aligned16(k) ||
-        !aligned16(v) || !aligned16(o))
+        !aligned16(v) || !aligned16(o) || !aligned16(valid))
         return fail(MAKO_EINVAL, "attention_sparse: null or unaligned argument");
     if (n_q == 0)
         return MAKO_OK;

@@ -248,6 +248,42 @@ def test_block_sparse_lists(ctx, oracle, kernel):
     ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 0)
 
 
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_block_sparse_irregular_lists(ctx, oracle, dtype):
+    """Lists of different lengths within a tile (the shorter one padded with empty passes), a repeated entry (counted
+    twice, as the reference's pass list does), entries >= n_cubes (skipped), an odd block count and GQA."""
+    import torch
+    heads, kv_heads, n = 4, 2, 1344  # 21 blocks: the last tile's second cube does not exist
+    nb = n // 64
+    rng = np.random.default_rng(90 + dtype)
+    max_list = 9
+    lists = rng.integers(0, nb, size=(heads, nb, max_list)).astype(np.int32)
+    counts = rng.integers(0, max_list + 1, size=(heads, nb)).astype(np.int32)
+    lists[0, 0, :3] = [5, 5, 5]
+    counts[0, 0] = 3
+    lists[1, 2, 1] = nb + 7  # out of range: skipped
+    lists[2, 4, 0] = 70000
+    counts[1, 2] = max(counts[1, 2], 2)
+    counts[2, 4] = max(counts[2, 4], 1)
+    counts[3, 5] = -4  # a negative count keeps nothing
+    case = C.dense_case(seed=91, heads=heads, kv_heads=kv_heads, dim=128, n_q=n, n_k=n, dtype=dtype)
+    case["k"], case["v"], case["k_pad"] = case["k"][:, :n], case["v"][:, :n], n  # this form's rows: [kv_heads][n]
+    q, k, v = dev(case["q"], dtype), dev(case["k"], dtype), dev(case["v"], dtype)
+    o = torch.full((n, heads * 128), SENTINEL, dtype=torch.float32, device="cuda")
+    ctx.attention_block_sparse(q, k, v, o, n, heads, kv_heads, dev_raw(lists), dev_raw(counts))
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    got = o.cpu().numpy()
+    sel = np.where(lists >= 0, np.minimum(lists, 65535), 65535).astype(np.uint16)
+    nsel = np.clip(counts, 0, None).astype(np.uint16)
+    want = oracle.attention_sparse(dtype, case["q"], case["k"], case["v"], n, case["q_pad"], n, case["k_pad"], heads,
+                                   kv_heads, heads * 128, nb, max_list, n, n, sel, nsel,
+                                   np.ones(case["k_pad"], np.uint8), np.arange(case["q_pad"], dtype=np.int32))[:n]
+    ok, stats = C.within(got, want)
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+    assert np.all(got[5 * 64:6 * 64, 3 * 128:4 * 128] == 0.0)
+
+
 def h3_layout(seed, frames, ph, pw, dense, heads, kv_heads, dtype):
     """A cube layout built the way H3::begin builds it (src/models/h3.cpp:510-546): 4x4x4 cubes over (frame, patch
     row, patch column) with partial cubes at the grid edges (their rows scattered, not leading), then the dense rows;
