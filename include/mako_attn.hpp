@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 namespace mako::attn {
 
@@ -72,16 +73,68 @@ public:
             throw std::runtime_error("attention: a kernel gave up on a pipeline wait (code " + std::to_string(err) + ")");
     }
     mako_attn_ctx* handle() const { return ctx_; }
+    void* stream() const { return stream_; }
+    int dtype() const { return dtype_; }
 
-private:
     static void check(int rc)
     {
         if (rc != MAKO_OK)
             throw std::runtime_error(mako_attn_last_error());
     }
+
+private:
     mako_attn_ctx* ctx_ = nullptr;
     void* stream_ = nullptr;
     int dtype_ = MAKO_F16;
+};
+
+// One process's member of a group of ranks on one box (no reference counterpart: mako-common drives one GPU).
+// `exchange` passes this rank's handle to every rank and returns all ranks' handles in rank order -- MPI_Allgather,
+// a torch.distributed all_gather_object, a file: whatever the host already uses to launch its ranks.
+class Group {
+public:
+    template <typename Exchange>
+    Group(Attention& attn, uint32_t rank, uint32_t n_ranks, uint32_t max_rows, Exchange&& exchange) : attn_(attn)
+    {
+        mako_ipc_handle mine;
+        Attention::check(mako_group_create(attn.handle(), rank, n_ranks, max_rows, &g_, &mine));
+        const std::vector<mako_ipc_handle> all = exchange(mine);
+        if (all.size() != n_ranks) {
+            mako_group_destroy(g_);
+            throw std::runtime_error("group: the exchange returned the wrong number of handles");
+        }
+        const int rc = mako_group_connect(g_, all.data());
+        if (rc != MAKO_OK) {
+            const std::string msg = mako_attn_last_error();
+            mako_group_destroy(g_);
+            throw std::runtime_error(msg);
+        }
+    }
+    ~Group() { mako_group_destroy(g_); }
+    Group(const Group&) = delete;
+    Group& operator=(const Group&) = delete;
+
+    // attention() for this rank's heads [head0, head0 + heads), each output row's slice stored into every rank's o
+    // (o_ranks: n_ranks pointers as this process addresses them, the others' mapped with mako_peer_open).
+    void attention_gather(const void* q, const void* k, const void* v, float* const* o_ranks, uint32_t n_q,
+                          uint32_t q_pad, uint32_t n_k, uint32_t k_pad, uint32_t heads, uint32_t kv_heads,
+                          uint32_t head0, uint32_t q_pos0, uint32_t block, uint32_t width)
+    {
+        Attention::check(mako_attention_gather(g_, attn_.stream(), attn_.dtype(), q, k, v, o_ranks, n_q, q_pad, n_k,
+                                               k_pad, heads, kv_heads, head0, q_pos0, block, width));
+    }
+    // attention_decode() over this rank's share of each sequence's keys, merged with the other ranks' shares.
+    void attention_decode_kv_sharded(const void* q, const void* k, const void* v, float* o, uint32_t batch,
+                                     const int32_t* kv_len, uint32_t max_kv_len, uint32_t heads, uint32_t kv_heads,
+                                     uint32_t dim, uint32_t k_stride)
+    {
+        Attention::check(mako_attention_decode_kv_sharded(g_, attn_.stream(), attn_.dtype(), q, k, v, o, batch, kv_len,
+                                                          max_kv_len, heads, kv_heads, dim, k_stride));
+    }
+
+private:
+    Attention& attn_;
+    mako_attn_group* g_ = nullptr;
 };
 
 } // namespace mako::attn

@@ -7,10 +7,14 @@
 #include <cstdio>
 #include <cstring>
 
-int main()
+int main(int argc, char**)
 {
     try {
         mako::attn::Attention attn(0);
+        if (argc > 100) {  // compiled, never run here: a one-rank group whose exchange is the identity
+            mako::attn::Group g(attn, 0, 1, 1, [](const mako_ipc_handle& h) { return std::vector<mako_ipc_handle>{h}; });
+            g.attention_decode_kv_sharded(nullptr, nullptr, nullptr, nullptr, 0, nullptr, 0, 1, 1, 128, 0);
+        }
         try {
             attn.attention(nullptr, nullptr, nullptr, nullptr, 1, 64, 1, 128, 1, 1, 0, 0, 96);
         } catch (const std::runtime_error& e) {
