@@ -42,6 +42,7 @@ constexpr long long WAIT_LIMIT = 1ll << 31;             // clock cycles (~1 s) b
 
 struct __align__(64) TcParams {
     CUtensorMap tq, tk, tv;
+    CUtensorMap to[8];  // head-sharded form: every destination o as [n_q][width] fp32, boxes of 128 rows x 32 floats
     float* od[8];   // output destinations (this rank's o, then the peers' mapped o for the head-sharded form)
     uint32_t n_od;  // destinations in od
     uint32_t head0;  // column of local head h: (head0 + h) * 128
@@ -58,6 +59,8 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// GATHER: the head-sharded form's epilogue (TMA stores into every rank's o); otherwise plain stores into p.od[0].
+template <bool GATHER>
 __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__ TcParams p)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -329,7 +332,48 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             atomicExch(p.err, 3);
         const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
         const uint32_t grow = q0 + x * TBM + row;
-        const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(p.head0 + h) * TD;
+        if (GATHER) {
+            // Head-sharded form: the tile's output goes through its Q buffer (free since its last Q.K^T) as 128-byte
+            // swizzled boxes of 128 rows x 32 floats, and TMA stores each box into every rank's o.  The stores run
+            // asynchronously -- the next CTA on this SM computes while they cross NVLink.  Two halves of 64 columns.
+            const uint32_t stage = sQ + x * TILE_BYTES;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    uint32_t o[32];
+                    if (ok && nb > 0) {
+                        tmem_ld32(tl + colO + (2 * half + cc) * 32, o);
+                        tmem_wait_ld();
+                        reg_fence(o);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            o[i] = 0u;
+                    }
+                    const uint32_t rbase = stage + cc * BOX_BYTES + row * 128;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(rbase + ((k ^ (row & 7)) * 16)),
+                                     "f"(__uint_as_float(o[4 * k]) * inv), "f"(__uint_as_float(o[4 * k + 1]) * inv),
+                                     "f"(__uint_as_float(o[4 * k + 2]) * inv), "f"(__uint_as_float(o[4 * k + 3]) * inv)
+                                     : "memory");
+                }
+                fence_proxy_async_smem();
+                named_bar(1 + x, 128);
+                if (row == 0) {
+                    for (uint32_t dI = 0; dI < p.n_od; ++dI)
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc)
+                            tma_store_2d(&p.to[dI], stage + cc * BOX_BYTES,
+                                         int((p.head0 + h) * TD + (2 * half + cc) * 32), int(q0 + x * TBM));
+                    bulk_commit();
+                    bulk_wait_read0();  // the staging buffer may be rewritten
+                }
+                named_bar(1 + x, 128);
+            }
+        } else {
+        const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(h) * TD;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -343,22 +387,15 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                     o[i] = 0u;
             }
             if (grow < p.n_q) {
+                float* orow = p.od[0] + ooff;
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    o[i] = __float_as_uint(__uint_as_float(o[i]) * inv);
-                // Head-sharded form: the same row slice into every rank's o (NVLink stores to the peers).
-                for (uint32_t dI = 0; dI < p.n_od; ++dI) {
-                    float* orow = p.od[dI] + ooff;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        *reinterpret_cast<float4*>(orow + c * 32 + i * 4) =
-                            make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
-                                        __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
-                }
+                for (int i = 0; i < 8; ++i)
+                    *reinterpret_cast<float4*>(orow + c * 32 + i * 4) =
+                        make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                    __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
             }
         }
-        if (p.n_od > 1)  // the peers' copies are performed before this rank's barrier releases them
-            __threadfence_system();
+        }
     }
     __syncwarp();
     fence_before();
@@ -471,6 +508,21 @@ bool head_map(CUtensorMap* map, const void* ptr, bool bf16, uint32_t rows, uint3
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// o [n_q][width] fp32 as a TMA store target: boxes of 128 rows x 32 floats (128 bytes, 128-byte swizzle).
+bool out_map(CUtensorMap* map, float* o, uint32_t n_q, uint32_t width)
+{
+    auto enc = encode_fn();
+    if (!enc)
+        return false;
+    cuuint64_t dims[2] = {width, n_q};
+    cuuint64_t strides[1] = {uint64_t(width) * 4};
+    cuuint32_t box[2] = {32, 128};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 } // namespace
 
 cudaError_t launch_v_to_f16(const void* v, void* v16, uint32_t* vmax, float* vinv, uint32_t kv_heads, uint32_t k_pad,
@@ -508,8 +560,11 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, const void* v16, cons
     } else {
         if (a.n_od > 8)
             return cudaErrorInvalidValue;
-        for (uint32_t i = 0; i < a.n_od; ++i)
+        for (uint32_t i = 0; i < a.n_od; ++i) {
             p.od[i] = a.od[i];
+            if (a.n_od > 1 && !out_map(&p.to[i], a.od[i], a.n_q, a.width))
+                return cudaErrorInvalidValue;
+        }
         p.n_od = a.n_od;
         p.head0 = a.head0;
     }
@@ -527,10 +582,12 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, const void* v16, cons
     p.width = a.width;
     p.n_tiles = (a.q_pad + 2 * TBM - 1) / (2 * TBM);
     p.scale_log2 = a.scale * kLog2e;
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL);
+    const bool gather = p.n_od > 1;
+    auto kern = gather ? attn_tc_kernel<true> : attn_tc_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL);
     if (e != cudaSuccess)
         return e;
-    attn_tc_kernel<<<dim3(p.n_tiles, a.heads), TNT, SMEM_TOTAL, st>>>(p);
+    kern<<<dim3(p.n_tiles, a.heads), TNT, SMEM_TOTAL, st>>>(p);
     return cudaGetLastError();
 }
 
