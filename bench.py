@@ -10,6 +10,7 @@ Workloads (synthetic seeded data -- no dataset is involve
   bidir          configs[4]: bidirectional bf16, 24 heads, D 128, N 75600, RMS-normalised q and k
   prefill_small  configs[0]: causal GQA prefill fp16, 16 / 8 heads, D 128, S 512
   decode_long    configs[1]'s variant: one sequence of 262144 fp16 keys, 32 / 8 heads, D 128
+  heads          the head-tile producers (RMS norm + RoPE into bf16 tiles) at configs[2]'s shape
 A step is one call of the public C ABI (include/mako_attn.h) over one batch held in HBM; `value` is device time
 (CUDA events on the launching stream, L2 flushed between steps, max over ranks); `e2e` is the same metric with the
 step's inputs copied from pinned host memory and its output read back inside the timed region.  With N > 1 the
@@ -450,6 +451,76 @@ class Sparse(Workload):
         return self.o.cpu().numpy()[rows], out[rows], f"{len(rows)} query rows x all heads"
 
 
+class Heads(Workload):
+    """Head-tile producers at configs[2]'s 8B-model shape: per sequence (batch 2, 8192 tokens) the q, k and v tiles
+    from fp32 projection rows -- q and k RMS-normed with their norm weights and rotated over all 128 values, v as is
+    -- into bf16 [heads][8192][128] tiles (TransformerRuntime::heads_partial, as src/models/qwen_text.cpp:415-417
+    calls it).  HBM-bound: bytes = fp32 rows read + bf16 tiles written + angle rows read."""
+    name, metric, unit, bound, dtype = "heads", "head-tile producer GB/s (RMS norm + RoPE)", "GB/s", "hbm", "bf16"
+
+    def __init__(self, seed=0):
+        import torch
+        self.B, self.T, self.H, self.KV, self.D = 2, 8192, 32, 8, 128
+        g = torch.Generator(device="cpu")
+        g.manual_seed(seed)
+        B, T, H, KV, D = self.B, self.T, self.H, self.KV, self.D
+        self.xq = torch.randn((B * T, H * D), generator=g).to(DEVICE)
+        self.xk = torch.randn((B * T, KV * D), generator=g).to(DEVICE)
+        self.xv = torch.randn((B * T, KV * D), generator=g).to(DEVICE)
+        pos = torch.arange(T, dtype=torch.float64)[:, None]
+        inv = 1.0 / (1.0e6 ** (torch.arange(D // 2, dtype=torch.float64) / (D // 2)))
+        ang = pos * inv[None, :]
+        self.cs = torch.stack([torch.cos(ang), torch.sin(ang)], -1).to(torch.float32).contiguous().to(DEVICE)
+        self.wq = (1.0 + 0.1 * torch.randn(D, generator=g)).to(DEVICE)
+        self.wk = (1.0 + 0.1 * torch.randn(D, generator=g)).to(DEVICE)
+        self.qh = torch.empty((B * H, T, D), dtype=torch.bfloat16, device=DEVICE)
+        self.kh = torch.empty((B * KV, T, D), dtype=torch.bfloat16, device=DEVICE)
+        self.vh = torch.empty((B * KV, T, D), dtype=torch.bfloat16, device=DEVICE)
+        self.inputs = [self.xq, self.xk, self.xv, self.cs, self.wq, self.wk]
+        self.outputs = [self.qh, self.kh, self.vh]
+        self.eps = 1e-6
+        self.config = {"workload": "heads (configs[2] shape: batch 2, 8192 tokens, 32 q / 8 kv heads, D 128)",
+                       "norm": "RMS on q and k (eps 1e-6)", "rotation": "all 128 values, halves", "tiles": "bf16",
+                       "calls_per_step": 6, "l2": "flushed between steps (256 MB write)"}
+
+    def work(self):
+        B, T, H, KV, D = self.B, self.T, self.H, self.KV, self.D
+        rows = B * T * (H + 2 * KV) * D
+        return float(rows * 4 + rows * 2 + 2 * B * T * (D // 2) * 8)  # x read, tiles written, angles (q, k calls)
+
+    def step(self, ctx):
+        B, T, H, KV, D = self.B, self.T, self.H, self.KV, self.D
+        for b in range(B):
+            rows = slice(b * T, (b + 1) * T)
+            ctx.heads_partial(self.xq[rows], H * D, 0, D, D, D, H, T, T, self.cs, self.wq, self.eps,
+                              self.qh[b * H:(b + 1) * H])
+            ctx.heads_partial(self.xk[rows], KV * D, 0, D, D, D, KV, T, T, self.cs, self.wk, self.eps,
+                              self.kh[b * KV:(b + 1) * KV])
+            ctx.heads_partial(self.xv[rows], KV * D, 0, D, D, 0, KV, T, T, None, None, 0.0,
+                              self.vh[b * KV:(b + 1) * KV])
+
+    def cpu_sample(self, O, threads, frac=1.0):
+        xq = self.xq[:self.T].cpu().numpy()
+        cs = self.cs.cpu().numpy()
+        wq = self.wq.cpu().numpy()
+        T, H, D = self.T, self.H, self.D
+
+        def run():
+            return O.heads(xq, H * D, 0, D, D, D, 1, T, H, T, cs=cs, cs_row=D // 2, w=wq, eps=self.eps)
+        rows = T * H * D
+        return run, float(rows * 6 + T * (D // 2) * 8), "the q tiles of sequence 0 (8192 tokens x 32 heads)"
+
+    def check(self, O):
+        import numpy as np
+        T, H, D = self.T, self.H, self.D
+        xq = self.xq[:T].cpu().numpy()
+        want = O.heads(xq, H * D, 0, D, D, D, 1, T, H, T, cs=self.cs.cpu().numpy(), cs_row=D // 2,
+                       w=self.wq.cpu().numpy(), eps=self.eps)
+        want = O.from_bits(O.to_bits(want, 1), 1)  # the oracle's values rounded to the tiles' bf16
+        got = self.qh[:H].float().cpu().numpy()
+        return got.reshape(H * T, D), want.reshape(H * T, D), "the q tiles of sequence 0 against the oracle in bf16"
+
+
 def torch_int16():
     import torch
     return torch.int16
@@ -473,6 +544,8 @@ def make_workload(name, world=1, rank=0):
                        0, rms_qk=True, cfg="bidir (configs[4])", world=world, rank=rank)
     if name == "sparse":
         return Sparse()
+    if name == "heads":
+        return Heads()
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -662,7 +735,7 @@ def run_mako(args):
     ctx.set_option(mako_attn.OPT_KERNEL_TIMING, 0)
     barrier(world)
     clk = clocks.stop()
-    kernel_ms = max_over_ranks(statistics.mean(kt), world) if kt else None
+    kernel_ms = max_over_ranks(sum(kt) / args.steps, world) if kt else None  # main kernels of one step
 
     hbm, tflops, src = peaks()
     call_ms = statistics.mean(ms)
@@ -679,7 +752,7 @@ def run_mako(args):
     roof["kernel_ms"] = round(per_launch_ms, 5)
     roof["call_ms"] = round(call_ms, 5)
     roof["timed"] = ("main kernel of each call (CUDA events the library records around it on the launching stream), "
-                     "mean over the steps" + (", max over ranks" if world > 1 else "")
+                     "summed per step, mean over the steps" + (", max over ranks" if world > 1 else "")
                      if kernel_ms else "whole C-ABI call per step")
     roof["work_per_launch"] = work
 
@@ -769,7 +842,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "decode_long", "prefill", "sparse", "bidir", "prefill_small"])
+                    choices=["decode", "decode_long", "prefill", "sparse", "bidir", "prefill_small", "heads"])
     ap.add_argument("--impl", default="mako", choices=["mako", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -143,6 +143,35 @@ int mako_attention_block_sparse(mako_attn_ctx* ctx, void* stream, int dtype, con
                                 const void* v, float* o, uint32_t n, uint32_t heads, uint32_t kv_heads,
                                 const int32_t* lists, const int32_t* counts, uint32_t max_list);
 
+/* ---- Head-tile producers: the 16-bit tiles the attention calls read, from fp32 projection rows ----------------
+ * y is [heads][n_pad][dim] of `dtype` (the reference writes half; MAKO_BF16 is offered for bf16 attention), 16-byte
+ * aligned like the attention tensors.  cs holds
+ * the rotation angles as (cos, sin) float pairs; x, cs and w are device fp32 arrays.  Calls are stream-ordered. */
+
+/* TransformerRuntime::heads (src/models/runtime.hpp:75-77, runtime.cpp:215-226; kernel heads_half, ops.metal:21-43):
+ * y[h][t][d] = x[t][col0 + h * 128 + d] for t < T, rotated when rope is 1 (halves, d with d + 64) or 2 (adjacent
+ * pairs) by cs[t][pair]; the rows [T, n_pad) are zeroed.  128-wide heads. */
+int mako_heads(mako_attn_ctx* ctx, void* stream, int dtype, const float* x, uint32_t ld, uint32_t col0,
+               uint32_t heads, uint32_t T, uint32_t n_pad, const float* cs, uint32_t rope, void* y);
+/* TransformerRuntime::heads_norm (runtime.hpp:78-81, runtime.cpp:228-241; kernel heads_norm_half,
+ * ops.metal:371-408): mako_heads with each head RMS-normed first (x / sqrt(mean(x^2) + eps) * w[d]), written at rows
+ * row0 .. row0 + T - 1; the other rows are left as they are. */
+int mako_heads_norm(mako_attn_ctx* ctx, void* stream, int dtype, const float* x, uint32_t ld, uint32_t col0,
+                    uint32_t heads, uint32_t T, uint32_t n_pad, const float* cs, uint32_t rope, const float* w,
+                    float eps, uint32_t row0, void* y);
+/* TransformerRuntime::heads_partial (runtime.hpp:82-87, runtime.cpp:243-260; kernel heads_partial,
+ * ops.metal:577-613): heads of `dim` (a multiple of 32, at most 256) at col0 + h * stride of each row, RMS-normed
+ * times w when w is given (eps), their first `rot` values rotated as halves (i with i + rot / 2) by cs[t][i]
+ * (rot / 2 pairs a row); with a map, y row r comes from x row map[r] and its angles (a zero row where map[r] < 0).
+ * Rejects what the reference rejects (dim > 256, dim % 32, odd rot) and, added, rot > dim. */
+int mako_heads_partial(mako_attn_ctx* ctx, void* stream, int dtype, const float* x, uint32_t ld, uint32_t col0,
+                       uint32_t stride, uint32_t dim, uint32_t rot, uint32_t heads, uint32_t T, uint32_t n_pad,
+                       const float* cs, const float* w, float eps, void* y, const int32_t* map);
+/* Kernel heads_clear (ops.metal:45-52), dispatched by the models after heads_partial (src/models/h3.cpp:352-356):
+ * zero the rows [from, n_pad) of every head of y [heads][n_pad][dim], so padded keys and values read as zeros. */
+int mako_heads_clear(mako_attn_ctx* ctx, void* stream, int dtype, void* y, uint32_t dim, uint32_t n_pad, uint32_t from,
+                     uint32_t heads);
+
 /* ---- Multi-GPU: one process per GPU of one box, the peers' memory mapped through CUDA IPC ------------------------
  * No reference counterpart: mako-common drives one Apple GPU.  BASELINE's sharded forms -- heads across GPUs with the
  * outputs gathered, and one long sequence's KV cache across GPUs with a log-sum-exp combine -- are built from these.

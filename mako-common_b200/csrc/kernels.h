@@ -71,6 +71,21 @@ void decode_plan(uint32_t max_len, uint32_t batch, uint32_t kv_heads, uint32_t h
                  uint32_t* chunk, uint32_t* n_splits);
 cudaError_t launch_decode(const DecodeParams& p, int dtype, int dim, cudaStream_t s);
 
+// Head-tile producers: y [heads][n_pad][dim] 16-bit, row row0 + r from x row map[r] (or r): head h's values at
+// x + row * ld + col0 + h * stride, RMS-normed times w when eps > 0, rotated when rope is 1 (halves i, i + rot / 2 over
+// the first rot values) or 2 (adjacent pairs over the whole head) by the (cos, sin) pairs cs + row * cs_row.
+struct HeadsParams {
+    const float* x;
+    const float* cs;   // float2 pairs
+    const float* w;    // [dim], when eps > 0
+    const int32_t* map;  // [rows] or null; < 0: a zero row
+    void* y;
+    uint64_t ld;
+    uint32_t col0, stride, dim, rot, rope, rows, heads, n_pad, row0, cs_row, vec4;
+    float eps;
+};
+cudaError_t launch_heads(const HeadsParams& p, int dtype, cudaStream_t s);
+
 // ---- multi-GPU exchange (one process per GPU, peers' memory mapped through CUDA IPC) ------------------------------
 
 constexpr uint32_t kMaxRanks = 8;

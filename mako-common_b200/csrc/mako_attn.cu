@@ -630,6 +630,160 @@ int mako_attention_block_sparse(mako_attn_ctx* ctx, void* stream, int dtype, con
 
 } // extern "C"
 
+// ---- head-tile producers --------------------------------------------------------------------------------------------
+
+namespace {
+
+int heads_common(mako_attn_ctx* ctx, void* stream, int dtype, mako::HeadsParams& p, const char* what)
+{
+    if (int rc = check_ctx(ctx, dtype))
+        return rc;
+    if (!p.x || !p.y || (p.rope && !p.cs) || (p.eps > 0.0f && !p.w) || !aligned16(p.y))
+        return fail(MAKO_EINVAL, "%s: null argument or unaligned tile (16-byte alignment)", what);
+    if (uint64_t(p.row0) + p.rows > p.n_pad)
+        return fail(MAKO_EINVAL, "%s: rows %u + %u beyond n_pad %u", what, p.row0, p.rows, p.n_pad);
+    if (!(p.eps >= 0.0f))
+        return fail(MAKO_EINVAL, "%s: eps %g", what, double(p.eps));
+    if (p.rows == 0 || p.heads == 0)
+        return MAKO_OK;
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    p.vec4 = ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && p.ld % 4 == 0 && p.col0 % 4 == 0 && p.stride % 4 == 0)
+                 ? 1u
+                 : 0u;
+    ctx->launches += 1;
+    auto st = static_cast<cudaStream_t>(stream);
+    KernelTimer t(ctx, st);
+    cudaError_t e = mako::launch_heads(p, dtype, st);
+    t.stop();
+    return launched(what, e);
+}
+
+int clear_rows(void* y, int dtype, uint32_t dim, uint32_t n_pad, uint32_t from, uint32_t heads, cudaStream_t st)
+{
+    if (from >= n_pad || heads == 0)
+        return MAKO_OK;
+    (void)dtype;  // both element types are 2 bytes
+    const size_t pitch = size_t(n_pad) * dim * 2;
+    cudaError_t e = cudaMemset2DAsync(static_cast<char*>(y) + size_t(from) * dim * 2, pitch, 0,
+                                      size_t(n_pad - from) * dim * 2, heads, st);
+    return e == cudaSuccess ? MAKO_OK : cuda_fail("heads_clear", e);
+}
+
+} // namespace
+
+extern "C" {
+
+int mako_heads(mako_attn_ctx* ctx, void* stream, int dtype, const float* x, uint32_t ld, uint32_t col0,
+               uint32_t heads, uint32_t T, uint32_t n_pad, const float* cs, uint32_t rope, void* y)
+{
+    if (rope > 2)
+        return fail(MAKO_EINVAL, "heads: rope %u (0 none, 1 halves, 2 adjacent pairs)", rope);
+    if (T > n_pad)
+        return fail(MAKO_EINVAL, "heads: %u rows beyond n_pad %u", T, n_pad);
+    mako::HeadsParams p{};
+    p.x = x;
+    p.cs = cs;
+    p.y = y;
+    p.ld = ld;
+    p.col0 = col0;
+    p.stride = 128;
+    p.dim = 128;
+    p.rot = 128;
+    p.rope = rope;
+    p.rows = T;
+    p.heads = heads;
+    p.n_pad = n_pad;
+    p.cs_row = 64;
+    if (int rc = heads_common(ctx, stream, dtype, p, "heads"))
+        return rc;
+    if (T < n_pad && heads && y) {
+        DeviceGuard dg(ctx->device);
+        return clear_rows(y, dtype, 128, n_pad, T, heads, static_cast<cudaStream_t>(stream));
+    }
+    return MAKO_OK;
+}
+
+int mako_heads_norm(mako_attn_ctx* ctx, void* stream, int dtype, const float* x, uint32_t ld, uint32_t col0,
+                    uint32_t heads, uint32_t T, uint32_t n_pad, const float* cs, uint32_t rope, const float* w,
+                    float eps, uint32_t row0, void* y)
+{
+    if (rope > 2)
+        return fail(MAKO_EINVAL, "heads_norm: rope %u (0 none, 1 halves, 2 adjacent pairs)", rope);
+    if (!(eps > 0.0f))
+        return fail(MAKO_EINVAL, "heads_norm: eps %g (positive)", double(eps));
+    mako::HeadsParams p{};
+    p.x = x;
+    p.cs = cs;
+    p.w = w;
+    p.y = y;
+    p.ld = ld;
+    p.col0 = col0;
+    p.stride = 128;
+    p.dim = 128;
+    p.rot = 128;
+    p.rope = rope;
+    p.rows = T;
+    p.heads = heads;
+    p.n_pad = n_pad;
+    p.row0 = row0;
+    p.cs_row = 64;
+    p.eps = eps;
+    return heads_common(ctx, stream, dtype, p, "heads_norm");
+}
+
+int mako_heads_partial(mako_attn_ctx* ctx, void* stream, int dtype, const float* x, uint32_t ld, uint32_t col0,
+                       uint32_t stride, uint32_t dim, uint32_t rot, uint32_t heads, uint32_t T, uint32_t n_pad,
+                       const float* cs, const float* w, float eps, void* y, const int32_t* map)
+{
+    // the reference's check and message (src/models/runtime.cpp:248-249), and rot within the head
+    if (dim > 256 || dim % 32 || rot % 2 || dim == 0)
+        return fail(MAKO_EINVAL, "heads_partial: heads of %u with %u rotated", dim, rot);
+    if (rot > dim)
+        return fail(MAKO_EINVAL, "heads_partial: %u rotated of a head of %u", rot, dim);
+    if (T > n_pad)
+        return fail(MAKO_EINVAL, "heads_partial: %u rows beyond n_pad %u", T, n_pad);
+    mako::HeadsParams p{};
+    p.x = x;
+    p.cs = cs;
+    p.w = w;
+    p.map = map;
+    p.y = y;
+    p.ld = ld;
+    p.col0 = col0;
+    p.stride = stride;
+    p.dim = dim;
+    p.rot = rot;
+    p.rope = rot ? 1u : 0u;
+    p.rows = T;
+    p.heads = heads;
+    p.n_pad = n_pad;
+    p.cs_row = rot / 2;
+    p.eps = w ? eps : 0.0f;  // the reference normalises only when w is given
+    if (w && !(eps > 0.0f))
+        return fail(MAKO_EINVAL, "heads_partial: eps %g with a norm weight", double(eps));
+    return heads_common(ctx, stream, dtype, p, "heads_partial");
+}
+
+int mako_heads_clear(mako_attn_ctx* ctx, void* stream, int dtype, void* y, uint32_t dim, uint32_t n_pad, uint32_t from,
+                     uint32_t heads)
+{
+    if (int rc = check_ctx(ctx, dtype))
+        return rc;
+    if (!y || !dim)
+        return fail(MAKO_EINVAL, "heads_clear: null tile or zero width");
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    int rc = clear_rows(y, dtype, dim, n_pad, from, heads, static_cast<cudaStream_t>(stream));
+    if (rc == MAKO_OK)
+        g_error.clear();
+    return rc;
+}
+
+} // extern "C"
+
 // ---- multi-GPU ------------------------------------------------------------------------------------------------------
 
 struct mako_attn_group {

@@ -23,7 +23,7 @@ SYMBOLS = (
     "mako_attention_block_sparse", "mako_attention_decode_noalloc",
     "mako_peer_alloc", "mako_peer_free", "mako_peer_open", "mako_peer_close", "mako_group_create", "mako_group_connect",
     "mako_group_destroy", "mako_attention_gather", "mako_attention_decode_kv_sharded", "mako_group_connect_ptrs",
-    "mako_group_area",
+    "mako_group_area", "mako_heads", "mako_heads_norm", "mako_heads_partial", "mako_heads_clear",
 )
 MAX_RANKS = 8
 
@@ -66,6 +66,11 @@ def lib():
     L.mako_attention_sparse.argtypes = [p, p, i32, p, p, p, p] + [u32] * 11 + [p, p, p, p]
     L.mako_attention_block_sparse.argtypes = [p, p, i32, p, p, p, p, u32, u32, u32, p, p, u32]
     L.mako_attention_decode_noalloc.argtypes = [p, i32, p, p, p, p, u32, p, u32, u32, u32, u32, u32]
+    f32 = ctypes.c_float
+    L.mako_heads.argtypes = [p, p, i32, p, u32, u32, u32, u32, u32, p, u32, p]
+    L.mako_heads_norm.argtypes = [p, p, i32, p, u32, u32, u32, u32, u32, p, u32, p, f32, u32, p]
+    L.mako_heads_partial.argtypes = [p, p, i32, p, u32, u32, u32, u32, u32, u32, u32, u32, p, p, f32, p, p]
+    L.mako_heads_clear.argtypes = [p, p, i32, p, u32, u32, u32, u32]
     H = ctypes.POINTER(IpcHandle)
     L.mako_peer_alloc.argtypes = [p, ctypes.c_size_t, ctypes.POINTER(p), H]
     L.mako_peer_free.argtypes = [p, p]
@@ -181,6 +186,23 @@ class Context:
         batch = kv_len.numel()
         _check(lib().mako_attention_decode(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(o),
                                            batch, _ptr(kv_len), max_kv_len, heads, kv_heads, dim, k_stride))
+
+    # -- TransformerRuntime::heads / heads_norm / heads_partial (src/models/runtime.cpp:215-260) and heads_clear;
+    # y is a float16 or bfloat16 tensor [heads][n_pad][dim], x / cs / w float32 tensors (cs: (cos, sin) pairs)
+    def heads(self, x, ld, col0, heads, T, n_pad, cs, rope, y, stream=None):
+        _check(lib().mako_heads(self._h, _stream(stream), dtype_code(y), _ptr(x), ld, col0, heads, T, n_pad, _ptr(cs),
+                                rope, _ptr(y)))
+
+    def heads_norm(self, x, ld, col0, heads, T, n_pad, cs, rope, w, eps, row0, y, stream=None):
+        _check(lib().mako_heads_norm(self._h, _stream(stream), dtype_code(y), _ptr(x), ld, col0, heads, T, n_pad,
+                                     _ptr(cs), rope, _ptr(w), eps, row0, _ptr(y)))
+
+    def heads_partial(self, x, ld, col0, stride, dim, rot, heads, T, n_pad, cs, w, eps, y, map_=None, stream=None):
+        _check(lib().mako_heads_partial(self._h, _stream(stream), dtype_code(y), _ptr(x), ld, col0, stride, dim, rot,
+                                        heads, T, n_pad, _ptr(cs), _ptr(w), eps, _ptr(y), _ptr(map_)))
+
+    def heads_clear(self, y, dim, n_pad, from_, heads, stream=None):
+        _check(lib().mako_heads_clear(self._h, _stream(stream), dtype_code(y), _ptr(y), dim, n_pad, from_, heads))
 
     # -- TransformerRuntime::cube_select (src/models/runtime.cpp:286-303); returns (sel, nsel) as int16 tensor views
     # of the context's scratch ([heads][n_cubes][min(topk, n_cubes)] and [heads][n_cubes], uint16 bit patterns),

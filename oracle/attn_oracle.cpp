@@ -350,4 +350,56 @@ void oracle_sparse_test_fixture(uint16_t* q, uint16_t* k, uint16_t* v, uint8_t* 
                 }
 }
 
+// Head-tile producers (TransformerRuntime::heads / heads_norm / heads_partial, src/models/runtime.cpp:215-260):
+// restates heads_half (src/kernels/ops.metal:21-43), heads_norm_half (:371-408) and heads_partial (:577-613) in
+// double.  y row row0 + r of head h takes x row map[r] (or r; a zero row where map[r] < 0) at col0 + h * stride:
+// RMS-normed over the head times w when eps > 0 (x / sqrt(sum(x^2) / dim + eps) * w[d]), then rotated when rope is
+// 1 (halves: i with i + rot / 2 over the first rot values, pair i % (rot / 2)) or 2 (adjacent pairs 2i, 2i + 1 over
+// the whole head, pair i) by the (cos, sin) pairs cs + t * cs_row: u' = u c - v s, v' = v c + u s.  y receives the
+// values before 16-bit rounding, [heads][n_pad][dim]; other rows are left as they are.
+void oracle_heads(const float* x, uint64_t ld, uint32_t col0, uint32_t stride, uint32_t dim, uint32_t rot,
+                  uint32_t rope, uint32_t rows, uint32_t heads, uint32_t n_pad, uint32_t row0, const float* cs,
+                  uint32_t cs_row, const float* w, float eps, const int32_t* map, float* y)
+{
+    std::vector<double> v(dim), o(dim);
+    for (uint32_t h = 0; h < heads; ++h)
+        for (uint32_t r = 0; r < rows; ++r) {
+            float* yr = y + (uint64_t(h) * n_pad + row0 + r) * dim;
+            const int64_t t = map ? int64_t(map[r]) : int64_t(r);
+            if (t < 0) {
+                std::fill(yr, yr + dim, 0.0f);
+                continue;
+            }
+            const float* xr = x + uint64_t(t) * ld + col0 + uint64_t(h) * stride;
+            for (uint32_t i = 0; i < dim; ++i)
+                v[i] = xr[i];
+            if (eps > 0.0f) {
+                double ss = 0.0;
+                for (uint32_t i = 0; i < dim; ++i)
+                    ss += v[i] * v[i];
+                const double inv = 1.0 / std::sqrt(ss / dim + double(eps));
+                for (uint32_t i = 0; i < dim; ++i)
+                    v[i] *= inv * double(w[i]);
+            }
+            o = v;
+            const float* c = cs ? cs + uint64_t(t) * cs_row * 2 : nullptr;
+            if (rope == 2) {
+                for (uint32_t i = 0; i + 1 < dim; i += 2) {
+                    const double cc = c[i], sn = c[i + 1];  // pair i / 2 at floats 2 (i / 2), 2 (i / 2) + 1
+                    o[i] = v[i] * cc - v[i + 1] * sn;
+                    o[i + 1] = v[i + 1] * cc + v[i] * sn;
+                }
+            } else if (rope == 1 && rot) {
+                const uint32_t half = rot / 2;
+                for (uint32_t i = 0; i < half; ++i) {
+                    const double cc = c[2 * i], sn = c[2 * i + 1];
+                    o[i] = v[i] * cc - v[i + half] * sn;
+                    o[i + half] = v[i + half] * cc + v[i] * sn;
+                }
+            }
+            for (uint32_t i = 0; i < dim; ++i)
+                yr[i] = float(o[i]);
+        }
+}
+
 } // extern "C"

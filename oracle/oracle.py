@@ -40,6 +40,8 @@ def lib():
         L.oracle_attention_sparse.argtypes = ([i32, ptr, ptr, ptr, ptr] + [u32] * 11 + [ptr] * 4 + [ptr, u32, i32])
         L.oracle_cube_select.argtypes = ([i32, ptr, ptr] + [u32] * 4 + [ptr] + [u32] * 3 + [i32] + [ptr] * 5)
         L.oracle_sparse_test_fixture.argtypes = [ptr] * 6
+        L.oracle_heads.argtypes = [ptr, ctypes.c_uint64] + [u32] * 9 + [ptr, u32, ptr, ctypes.c_float, ptr, ptr]
+        L.oracle_heads.restype = None
         for f in (L.oracle_attention, L.oracle_decode, L.oracle_attention_sparse, L.oracle_cube_select,
                   L.oracle_sparse_test_fixture):
             f.restype = None
@@ -209,3 +211,20 @@ def merge_partials(parts):
         acc += o * w[..., None]
     out = np.where(tot[..., None] > 0, acc / np.where(tot > 0, tot, 1.0)[..., None], 0.0)
     return out.reshape(out.shape[0], -1).astype(np.float32)
+
+
+# ---- head-tile producers ------------------------------------------------------------------------------------------
+
+def heads(x, ld, col0, stride, dim, rot, rope, rows, heads_, n_pad, row0=0, cs=None, cs_row=0, w=None, eps=0.0,
+          map_=None, out=None):
+    """heads_half / heads_norm_half / heads_partial restated (attn_oracle.cpp: oracle_heads); returns the float32
+    values [heads][n_pad][dim] before 16-bit rounding (rows not written stay as `out` had them, or 0)."""
+    x = _c(x, np.float32)
+    y = np.zeros((heads_, n_pad, dim), np.float32) if out is None else out
+    assert y.dtype == np.float32 and y.flags.c_contiguous
+    cs = None if cs is None else _c(cs, np.float32)
+    w = None if w is None else _c(w, np.float32)
+    m = None if map_ is None else _c(map_, np.int32)
+    lib().oracle_heads(_p(x), ld, col0, stride, dim, rot, rope, rows, heads_, n_pad, row0, _p(cs), cs_row, _p(w),
+                       eps, _p(m), _p(y))
+    return y

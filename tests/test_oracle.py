@@ -180,3 +180,38 @@ def test_golden_vectors(oracle):
     oracle.attention_sparse(0, fx["q"], fx["k"], fx["v"], 444, 448, 444, 512, 2, 2, 256, 6, 3, 384, 444, sel, nsel,
                             fx["valid"], fx["map"], out=o)
     np.testing.assert_allclose(o[g["o_rows"]], g["o_sub"], rtol=0, atol=1e-6)
+
+
+def test_heads_oracle_matches_numpy(oracle):
+    """The producers' restatement against an independent numpy float64 one, with known-answer cases: a rotation by
+    zero is the identity, by a right angle turns (u, v) into (-v, u), and the RMS norm with unit weights gives unit
+    RMS rows."""
+    import numpy as np
+    rng = np.random.default_rng(3)
+    T, H, dim, stride, col0, rot = 6, 2, 64, 80, 8, 48
+    ld = col0 + stride * H
+    x = rng.standard_normal((T, ld)).astype(np.float32)
+    a = rng.uniform(-3, 3, (T, rot // 2))
+    cs = np.stack([np.cos(a), np.sin(a)], -1).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, dim).astype(np.float32)
+    got = oracle.heads(x, ld, col0, stride, dim, rot, 1, T, H, 8, cs=cs, cs_row=rot // 2, w=w, eps=1e-6)
+    for h in range(H):
+        v = x[:, col0 + h * stride: col0 + h * stride + dim].astype(np.float64)
+        v = v / np.sqrt((v * v).mean(-1, keepdims=True) + 1e-6) * w
+        o = v.copy()
+        c, s = cs[..., 0].astype(np.float64), cs[..., 1].astype(np.float64)
+        o[:, :rot // 2] = v[:, :rot // 2] * c - v[:, rot // 2:rot] * s
+        o[:, rot // 2:rot] = v[:, rot // 2:rot] * c + v[:, :rot // 2] * s
+        np.testing.assert_allclose(got[h, :T], o, rtol=1e-6, atol=1e-6)
+    # identity rotation, right-angle rotation, unit RMS
+    zero = np.zeros((T, 32, 2), np.float32)
+    zero[..., 0] = 1.0
+    y0 = oracle.heads(x, ld, 0, 64, 64, 64, 1, T, 1, T, cs=zero, cs_row=32)
+    np.testing.assert_array_equal(y0[0], x[:, :64])
+    quarter = np.zeros((T, 32, 2), np.float32)
+    quarter[..., 1] = 1.0
+    yq = oracle.heads(x, ld, 0, 64, 64, 64, 2, T, 1, T, cs=quarter, cs_row=32)
+    np.testing.assert_allclose(yq[0][:, 0::2], -x[:, 1:64:2], atol=1e-6)
+    np.testing.assert_allclose(yq[0][:, 1::2], x[:, 0:64:2], atol=1e-6)
+    yn = oracle.heads(x, ld, 0, 64, 64, 0, 0, T, 1, T, w=np.ones(64, np.float32), eps=1e-12)
+    np.testing.assert_allclose(np.sqrt((yn[0].astype(np.float64) ** 2).mean(-1)), 1.0, rtol=1e-6)
