@@ -63,6 +63,30 @@ public:
         check(mako_attention_decode(ctx_, stream_, dtype_, q, k, v, o, batch, kv_len, max_kv_len, heads, kv_heads, dim,
                                     k_stride));
     }
+    // TransformerRuntime::heads_partial (src/models/runtime.hpp:82-87): y 16-bit tiles of this object's dtype.
+    void heads_partial(const float* x, uint32_t ld, uint32_t col0, uint32_t stride, uint32_t dim, uint32_t rot,
+                       uint32_t heads, uint32_t T, uint32_t n_pad, const float* cs, const float* w, float eps, void* y,
+                       const int32_t* map = nullptr)
+    {
+        check(mako_heads_partial(ctx_, stream_, dtype_, x, ld, col0, stride, dim, rot, heads, T, n_pad, cs, w, eps, y,
+                                 map));
+    }
+    // TransformerRuntime::heads (runtime.hpp:75-77) and heads_norm (:78-81).
+    void heads(const float* x, uint32_t ld, uint32_t col0, uint32_t heads, uint32_t T, uint32_t n_pad, const float* cs,
+               uint32_t rope, void* y)
+    {
+        check(mako_heads(ctx_, stream_, dtype_, x, ld, col0, heads, T, n_pad, cs, rope, y));
+    }
+    void heads_norm(const float* x, uint32_t ld, uint32_t col0, uint32_t heads, uint32_t T, uint32_t n_pad,
+                    const float* cs, uint32_t rope, const float* w, float eps, uint32_t row0, void* y)
+    {
+        check(mako_heads_norm(ctx_, stream_, dtype_, x, ld, col0, heads, T, n_pad, cs, rope, w, eps, row0, y));
+    }
+    // The heads_clear dispatch (ops.metal:45-52): zero rows [from, n_pad) of every head.
+    void heads_clear(void* y, uint32_t dim, uint32_t n_pad, uint32_t from, uint32_t heads)
+    {
+        check(mako_heads_clear(ctx_, stream_, dtype_, y, dim, n_pad, from, heads));
+    }
     // The check gpu::Runtime::finish makes after a command buffer (src/gpu/runtime.cpp:466-471): throws if a
     // pipelined kernel gave up on a wait.  Synchronises the device.
     void finish()
