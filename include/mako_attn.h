@@ -134,6 +134,21 @@ int mako_attention_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const voi
                           uint32_t dense1, const uint16_t* sel, const uint16_t* nsel, const uint8_t* valid,
                           const int32_t* map);
 
+/* The cube layout of MiniMax-H3's sparse attention (src/models/h3.cpp:510-546; host code, host arrays): the video
+ * tokens of `frames` frames of ph x pw patches in 4 x 4 x 4 cubes of (frame, patch row, patch column), the grid padded
+ * to multiples of 4 with rows that are no token, then `dense` other rows.  Tile row r of the layout is model row
+ * map[r] (video token (f, y, x) is model row video_row0 + f * rows_per_frame + y * pw + x, dense row i is model row i;
+ * -1 for padding), valid[r] = 1 for tokens, cnt[c] = the tokens of cube c.  info receives the cube count, the rows,
+ * q_pad (a multiple of 64) and k_pad (of 128) -- the sizes of map and valid --, the dense range, topk =
+ * max(1, ceil(keep * n_cubes)) and the frame-slab stride for cube_select's `local` option.  With null arrays only info
+ * is filled.  Rejects more than 4096 cubes with the reference's message. */
+typedef struct {
+    uint32_t n_cubes, rows, q_pad, k_pad, dense0, dense1, topk, stride;
+} mako_cube_layout_info;
+int mako_cube_layout(uint32_t frames, uint32_t ph, uint32_t pw, uint32_t rows_per_frame, uint32_t video_row0,
+                     uint32_t dense, float keep, int32_t* map, uint8_t* valid, uint32_t* cnt,
+                     mako_cube_layout_info* info);
+
 /* Block-sparse attention from kept-block lists: n rows (a multiple of 64) of 64-row blocks, query block t of head
  * h attends the key blocks lists[h][t][0 .. counts[h][t]) (int32 device arrays, [heads][n / 64][max_list] and
  * [heads][n / 64]); every key valid, output row r to o row r (width heads * 128).  The same kernel as

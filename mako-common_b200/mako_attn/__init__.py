@@ -24,7 +24,14 @@ SYMBOLS = (
     "mako_peer_alloc", "mako_peer_free", "mako_peer_open", "mako_peer_close", "mako_group_create", "mako_group_connect",
     "mako_group_destroy", "mako_attention_gather", "mako_attention_decode_kv_sharded", "mako_group_connect_ptrs",
     "mako_group_area", "mako_heads", "mako_heads_norm", "mako_heads_partial", "mako_heads_clear",
+    "mako_cube_layout",
 )
+
+
+class CubeLayoutInfo(ctypes.Structure):
+    """mako_cube_layout_info."""
+    _fields_ = [(n, ctypes.c_uint32) for n in ("n_cubes", "rows", "q_pad", "k_pad", "dense0", "dense1", "topk",
+                                               "stride")]
 MAX_RANKS = 8
 
 
@@ -71,6 +78,7 @@ def lib():
     L.mako_heads_norm.argtypes = [p, p, i32, p, u32, u32, u32, u32, u32, p, u32, p, f32, u32, p]
     L.mako_heads_partial.argtypes = [p, p, i32, p, u32, u32, u32, u32, u32, u32, u32, u32, p, p, f32, p, p]
     L.mako_heads_clear.argtypes = [p, p, i32, p, u32, u32, u32, u32]
+    L.mako_cube_layout.argtypes = [u32] * 6 + [ctypes.c_float, p, p, p, ctypes.POINTER(CubeLayoutInfo)]
     H = ctypes.POINTER(IpcHandle)
     L.mako_peer_alloc.argtypes = [p, ctypes.c_size_t, ctypes.POINTER(p), H]
     L.mako_peer_free.argtypes = [p, p]
@@ -317,3 +325,19 @@ class Group:
         _check(lib().mako_attention_decode_kv_sharded(self._h, _stream(stream), dtype_code(q), _ptr(q), _ptr(k),
                                                       _ptr(v), _ptr(o), kv_len.numel(), _ptr(kv_len), max_kv_len,
                                                       heads, kv_heads, dim, k_stride))
+
+
+def cube_layout(frames, ph, pw, rows_per_frame, video_row0, dense, keep):
+    """mako_cube_layout: (map int32 [q_pad], valid uint8 [k_pad], cnt uint32 [n_cubes], info) as numpy arrays."""
+    import numpy as np
+    info = CubeLayoutInfo()
+    L = lib()
+    _check(L.mako_cube_layout(frames, ph, pw, rows_per_frame, video_row0, dense, keep, None, None, None,
+                              ctypes.byref(info)))
+    map_ = np.empty(info.q_pad, np.int32)
+    valid = np.empty(info.k_pad, np.uint8)
+    cnt = np.empty(max(info.n_cubes, 1), np.uint32)
+    _check(L.mako_cube_layout(frames, ph, pw, rows_per_frame, video_row0, dense, keep,
+                              map_.ctypes.data_as(ctypes.c_void_p), valid.ctypes.data_as(ctypes.c_void_p),
+                              cnt.ctypes.data_as(ctypes.c_void_p), ctypes.byref(info)))
+    return map_, valid, cnt[:info.n_cubes], info
