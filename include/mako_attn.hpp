@@ -161,4 +161,28 @@ private:
     mako_attn_group* g_ = nullptr;
 };
 
+// The cube layout of a video sequence for the sparse path (src/models/h3.cpp:510-546): host arrays to copy to the
+// device (map [q_pad], valid [k_pad], cnt [n_cubes]) and the sizes the sparse calls take.  Throws as the reference
+// does past 4096 cubes.
+struct CubeLayout {
+    mako_cube_layout_info info{};
+    std::vector<int32_t> map;
+    std::vector<uint8_t> valid;
+    std::vector<uint32_t> cnt;
+};
+
+inline CubeLayout cube_layout(uint32_t frames, uint32_t ph, uint32_t pw, uint32_t rows_per_frame,
+                              uint32_t video_row0, uint32_t dense, float keep)
+{
+    CubeLayout c;
+    Attention::check(mako_cube_layout(frames, ph, pw, rows_per_frame, video_row0, dense, keep, nullptr, nullptr,
+                                      nullptr, &c.info));
+    c.map.resize(c.info.q_pad);
+    c.valid.resize(c.info.k_pad);
+    c.cnt.resize(c.info.n_cubes);
+    Attention::check(mako_cube_layout(frames, ph, pw, rows_per_frame, video_row0, dense, keep, c.map.data(),
+                                      c.valid.data(), c.cnt.data(), &c.info));
+    return c;
+}
+
 } // namespace mako::attn

@@ -9,6 +9,13 @@
 
 int main(int argc, char**)
 {
+    // host code, no device needed: 3 x 10 x 10 patches -> 1 x 3 x 3 cubes, 50 dense rows after them
+    const auto lay = mako::attn::cube_layout(3, 10, 10, 100, 50, 50, 0.15f);
+    if (lay.info.n_cubes != 9 || lay.info.dense0 != 576 || lay.map.size() != 640 || lay.map[0] != 50 ||
+        lay.cnt[2] != 24) {
+        std::printf("cube_layout: unexpected layout\n");
+        return 1;
+    }
     try {
         mako::attn::Attention attn(0);
         if (argc > 100) {  // compiled, never run here: a one-rank group whose exchange is the identity
