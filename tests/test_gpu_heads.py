@@ -145,3 +145,63 @@ def test_heads_clear_and_errors(ctx):
         ctx.heads_partial(x, 128, 0, 128, 128, 3, 1, 1, 64, x, None, 0.0, y)
     with pytest.raises(mako_attn.MakoError, match="beyond n_pad"):
         ctx.heads_partial(x, 128, 0, 128, 128, 0, 1, 65, 64, None, None, 0.0, y)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_h3_sparse_block(ctx, oracle, dtype):
+    """One sparse attention block of H3 (src/models/h3.cpp:343-362) on a layout from mako_cube_layout: fp32 qkv rows
+    -> heads_partial through the cube map (q and k RMS-normed, 96 of 128 values rotated; v plain) -> heads_clear of
+    the tiles' padding rows -> cube_select with local = 3 and the layout's frame-slab stride -> attention_sparse back
+    into model row order.  Partial cubes at every grid edge and 63 dense rows.  Each stage is checked against the
+    oracle on the device's own inputs: tiles within one ulp, selection bit for bit, output within the attention
+    tolerance, every model row written and rows past them untouched."""
+    import torch
+    import mako_attn
+    rng = np.random.default_rng(300 + dtype)
+    frames, ph, pw, dense, H = 5, 10, 12, 63, 4
+    rpf = ph * pw
+    m, valid, cnt, L = mako_attn.cube_layout(frames, ph, pw, rpf, dense, dense, 0.25)
+    assert (L.n_cubes, L.topk, L.stride) == (18, 5, 9)
+    S, rows, q_pad, k_pad = dense + frames * rpf, L.rows, L.q_pad, L.k_pad
+    ld = 3 * H * 128
+    x = (rng.standard_normal((S, ld)) * 2.0).astype(np.float32)
+    cs = angles(rng, S, 48)
+    wq, wk = (rng.uniform(0.5, 1.5, 128).astype(np.float32) for _ in range(2))
+    tiles = [y_tile(H, q_pad, 128, dtype), y_tile(H, k_pad, 128, dtype), y_tile(H, k_pad, 128, dtype)]
+    args = [(0, 96, q_pad, wq, 1e-6), (H * 128, 96, k_pad, wk, 1e-6), (2 * H * 128, 0, k_pad, None, 0.0)]
+    xd, csd, md = tdev(x), tdev(cs), tdev(m)
+    for t, (col0, rot, n_pad, w, eps) in zip(tiles, args):
+        ctx.heads_partial(xd, ld, col0, 128, 128, rot, H, rows, n_pad, csd if rot else None,
+                          tdev(w) if w is not None else None, eps, t, md)
+        ctx.heads_clear(t, 128, n_pad, rows, H)
+    torch.cuda.synchronize()
+    tb = [bits(t) for t in tiles]
+    for got, (col0, rot, n_pad, w, eps) in zip(tb, args):
+        want = oracle.heads(x, ld, col0, 128, 128, rot, 1 if rot else 0, rows, H, n_pad, cs=cs, cs_row=48, w=w,
+                            eps=eps, map_=m)
+        far, exact = ulp_check(got[:, :rows], want[:, :rows], dtype)
+        assert far == 0 and exact >= 0.99, f"{far} elements beyond one ulp, {exact:.4f} bit-identical"
+        assert np.all(got[:, rows:] == 0)
+    qt, kt, vt = tiles
+    sel_t, nsel_t = ctx.cube_select(qt, kt, H, q_pad, k_pad, L.n_cubes, tdev(cnt), L.topk, 3, L.stride)
+    torch.cuda.synchronize()
+    sel = sel_t.cpu().numpy().view(np.uint16)
+    nsel = nsel_t.cpu().numpy().view(np.uint16)
+    want_sel, want_nsel, *_ = oracle.cube_select(dtype, tb[0], tb[1], H, q_pad, k_pad, L.n_cubes, cnt, L.topk,
+                                                 local=3, stride=L.stride, mode=1)
+    np.testing.assert_array_equal(sel, want_sel)
+    np.testing.assert_array_equal(nsel, want_nsel)
+    width = H * 128
+    o = torch.full((S + 2, width), 12345.0, dtype=torch.float32, device="cuda")
+    ctx.attention_sparse(qt, kt, vt, o, rows, q_pad, rows, k_pad, H, H, width, L.n_cubes, L.topk, L.dense0, L.dense1,
+                         sel_t, nsel_t, tdev(valid), md)
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    got = o.cpu().numpy()
+    want = np.full((S + 2, width), 12345.0, np.float32)
+    oracle.attention_sparse(dtype, tb[0], tb[1], tb[2], rows, q_pad, rows, k_pad, H, H, width, L.n_cubes, L.topk,
+                            L.dense0, L.dense1, sel, nsel, valid, m, out=want)
+    assert not np.any(want[:S] == 12345.0), "the layout maps every model row"
+    ok, stats = C.within(got[:S], want[:S])
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+    assert np.all(got[S:] == 12345.0)

@@ -285,29 +285,13 @@ def test_block_sparse_irregular_lists(ctx, oracle, dtype):
 
 
 def h3_layout(seed, frames, ph, pw, dense, heads, kv_heads, dtype):
-    """A cube layout built the way H3::begin builds it (src/models/h3.cpp:510-546): 4x4x4 cubes over (frame, patch
-    row, patch column) with partial cubes at the grid edges (their rows scattered, not leading), then the dense rows;
-    map sends each tile row to its model row (video rows after the dense ones)."""
+    """A cube layout as H3 builds it (src/models/h3.cpp:510-546), from the library's mako_cube_layout: 4x4x4 cubes
+    over (frame, patch row, patch column) with partial cubes at the grid edges (their rows scattered, not leading),
+    then the dense rows; map sends each tile row to its model row (video rows after the dense ones)."""
+    import mako_attn
     rng = np.random.default_rng(seed)
-    fc, yc, xc = -(-frames // 4), -(-ph // 4), -(-pw // 4)
-    n_cubes = fc * yc * xc
-    vrows = n_cubes * 64
-    rows = vrows + dense
-    q_pad, k_pad = C.round_up(rows, 64), C.round_up(rows, 128)
-    valid = np.zeros(k_pad, np.uint8)
-    map_ = np.full(q_pad, -1, np.int32)
-    cnt = np.zeros(n_cubes, np.uint32)
-    for f in range(frames):
-        for y in range(ph):
-            for x in range(pw):
-                cube = ((f // 4) * yc + y // 4) * xc + x // 4
-                r = cube * 64 + ((f % 4) * 4 + y % 4) * 4 + x % 4
-                map_[r] = dense + (f * ph + y) * pw + x
-                valid[r] = 1
-                cnt[cube] += 1
-    for r in range(dense):
-        map_[vrows + r] = r
-        valid[vrows + r] = 1
+    map_, valid, cnt, info = mako_attn.cube_layout(frames, ph, pw, ph * pw, dense, dense, 0.15)
+    n_cubes, vrows, rows, q_pad, k_pad = info.n_cubes, info.dense0, info.rows, info.q_pad, info.k_pad
     x = C.normal(rng, (3, max(heads, kv_heads), k_pad, 128)) * valid[None, None, :, None]
     q = oracle_bits(x[0, :heads, :q_pad], dtype)
     k = oracle_bits(x[1, :kv_heads], dtype)
