@@ -3,8 +3,8 @@
 // heads_partial (src/models/runtime.cpp:215-260; kernels heads_half, heads_norm_half, heads_partial,
 // src/kernels/ops.metal:11-43,371-408,577-613) -- and heads_clear (ops.metal:45-52).
 //
-// HBM-bound: a warp takes one output row of up to 4 heads, each lane dim / 32 consecutive values of each (128-bit
-// loads for 128-wide heads, the 4 heads' loads in flight together, the row's angles and the norm weights read once);
+// HBM-bound: a warp takes one output row of up to 8 heads, each lane dim / 32 consecutive values of each (128-bit
+// loads for 128-wide heads, the 8 heads' loads in flight together, the row's angles and the norm weights read once);
 // a head's sum of squares is a warp reduction; rotation partners (i with i + rot / 2, or 2i with 2i + 1) come from
 // the same lane, a shuffle, or a per-warp shared-memory copy of the row when the pairing crosses lanes unevenly.
 #include "kernels.h"
@@ -30,7 +30,12 @@ __device__ __forceinline__ __nv_bfloat16 to16<__nv_bfloat16>(float v)
     return __float2bfloat16_rn(v);
 }
 
-constexpr int HPW = 4;  // heads a warp takes (their loads in flight together; angles and weights read once)
+#ifndef MAKO_HEADS_HPW
+#define MAKO_HEADS_HPW 8
+#endif
+// heads a warp takes of its row: their loads are in flight together, and the row's angles and the norm weights are
+// read once for all of them
+constexpr int HPW = MAKO_HEADS_HPW;
 
 // VPL values a lane as 16-bit, packed into as few stores as the width allows.
 template <int VPL, typename T>
