@@ -5,7 +5,7 @@
 //
 // HBM-bound: a warp takes one output row of up to 8 heads, each lane dim / 32 consecutive values of each (128-bit
 // loads for 128-wide heads, the 8 heads' loads in flight together, the row's angles and the norm weights read once);
-// a head's sum of squares is a warp reduction; rotation partners (i with i + rot / 2, or 2i with 2i + 1) come from
+// a head's sum of squares is a warp reduction (the row's heads reduce interleaved); rotation partners (i with i + rot / 2, or 2i with 2i + 1) come from
 // the same lane, a shuffle, or a per-warp shared-memory copy of the row when the pairing crosses lanes unevenly.
 #include "kernels.h"
 
@@ -64,16 +64,14 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[VPL])
     }
 }
 
-template <int VPL, typename T>
-__global__ void __launch_bounds__(HW * 32, VPL <= 4 ? 4 : 2) heads_kernel(const HeadsParams p)
+// The rest of row r (model row t) once the values of its nh heads from h0 are in registers: RMS norm, rotation and
+// the 16-bit stores (zeros for t < 0).  cs: the row's angles (global or shared memory), wv: the norm weights of this
+// lane's values, buf: dim floats of per-warp scratch, used when rotation partners cross lanes unevenly.
+template <int VPL, int NH, typename T>
+__device__ __forceinline__ void row_out(const HeadsParams& p, int32_t t, uint32_t r, uint32_t h0, uint32_t nh,
+                                        float (&v)[NH][VPL], const float (&wv)[VPL], const float2* cs, float* buf,
+                                        int lane)
 {
-    __shared__ float row_buf[HW][VPL * 32];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t r = blockIdx.x * HW + warp, h0 = blockIdx.y * HPW;
-    if (r >= p.rows)
-        return;
-    const uint32_t nh = min(uint32_t(HPW), p.heads - h0);
-    const int32_t t = p.map ? p.map[r] : int32_t(r);
     T* const y0 = static_cast<T*>(p.y) + (uint64_t(h0) * p.n_pad + p.row0 + r) * p.dim + lane * VPL;
     const uint64_t ystep = uint64_t(p.n_pad) * p.dim;
     if (t < 0) {  // a row the map leaves empty is zero
@@ -85,110 +83,147 @@ __global__ void __launch_bounds__(HW * 32, VPL <= 4 ? 4 : 2) heads_kernel(const 
             store16<VPL, T>(y0 + j * ystep, z);
         return;
     }
-    // all the warp's heads of this row in flight at once
-    const float* const x0 = p.x + uint64_t(t) * p.ld + p.col0 + uint64_t(h0) * p.stride + lane * VPL;
-    float v[HPW][VPL];
-#pragma unroll
-    for (int j = 0; j < HPW; ++j) {
-        if (uint32_t(j) < nh) {
-            if (VPL % 4 == 0 && p.vec4) {
-#pragma unroll
-                for (int k = 0; k < VPL; k += 4) {
-                    const float4 w = __ldg(reinterpret_cast<const float4*>(x0 + j * p.stride + k));
-                    v[j][k] = w.x;
-                    v[j][k + 1] = w.y;
-                    v[j][k + 2] = w.z;
-                    v[j][k + 3] = w.w;
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < VPL; ++k)
-                    v[j][k] = __ldg(x0 + j * p.stride + k);
-            }
-        }
-    }
-    // per-row constants: norm weights and the angles of this lane's values
-    float wv[VPL], cc[VPL], sn[VPL];
-    if (p.eps > 0.0f)
-#pragma unroll
-        for (int k = 0; k < VPL; ++k)
-            wv[k] = __ldg(p.w + lane * VPL + k);
+    // the angles of this lane's values (value i < rot pairs with i +- rot / 2, or 2i with 2i + 1)
+    float cc[VPL], sn[VPL];
     const uint32_t half = p.rot / 2;
     if (p.rope) {
-        const float2* const cs = reinterpret_cast<const float2*>(p.cs) + uint64_t(t) * p.cs_row;
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
             const uint32_t i = lane * VPL + k;
             float2 c = make_float2(1.0f, 0.0f);
             if (p.rope == 2)
-                c = __ldg(cs + i / 2);
+                c = cs[i / 2];
             else if (i < p.rot)
-                c = __ldg(cs + i % half);
+                c = cs[i < half ? i : i - half];
             // the sign of the partner's term: -s for the first of a pair, +s for the second
             const bool first = p.rope == 2 ? (i & 1) == 0 : i < half;
             cc[k] = c.x;
             sn[k] = first ? -c.y : c.y;
         }
     }
-    // rotation partners: within the lane (adjacent pairs, even VPL), a fixed lane away (halves whose offset is a
-    // whole number of lanes), or through shared memory otherwise
-    const bool in_lane = p.rope == 2 && VPL % 2 == 0;
-    const bool by_shfl = p.rope == 1 && half % VPL == 0;
-    const int hl = int(half / VPL), src = lane < hl ? lane + hl : lane - hl;
+    // Every step runs over all NH heads at once (heads past nh hold zeros and are not stored), so the heads' shuffle
+    // chains overlap instead of following one another.
 #pragma unroll
-    for (int j = 0; j < HPW; ++j) {
+    for (int j = 0; j < NH; ++j)
         if (uint32_t(j) >= nh)
-            break;
-        float u[VPL];
-#pragma unroll
-        for (int k = 0; k < VPL; ++k)
-            u[k] = v[j][k];
-        if (p.eps > 0.0f) {  // RMS norm over the head, times w
-            float ss = 0.0f;
 #pragma unroll
             for (int k = 0; k < VPL; ++k)
-                ss = fmaf(u[k], u[k], ss);
+                v[j][k] = 0.0f;
+    if (p.eps > 0.0f) {  // RMS norm over each head, times w
+        float ss[NH];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-                ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float inv = rsqrtf(ss / float(p.dim) + p.eps);
+        for (int j = 0; j < NH; ++j) {
+            ss[j] = 0.0f;
 #pragma unroll
             for (int k = 0; k < VPL; ++k)
-                u[k] *= inv * wv[k];
+                ss[j] = fmaf(v[j][k], v[j][k], ss[j]);
         }
-        if (p.rope) {
-            float q[VPL];
-            if (in_lane) {
 #pragma unroll
-                for (int k = 0; k < VPL; ++k)
-                    q[k] = u[k ^ 1];
-            } else if (by_shfl) {
+        for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-                for (int k = 0; k < VPL; ++k)
-                    q[k] = __shfl_sync(0xffffffffu, u[k], src);
-            } else {
-                float* const buf = row_buf[warp];
+            for (int j = 0; j < NH; ++j)
+                ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], o);
+#pragma unroll
+        for (int j = 0; j < NH; ++j) {
+            const float inv = rsqrtf(ss[j] / float(p.dim) + p.eps);
+#pragma unroll
+            for (int k = 0; k < VPL; ++k)
+                v[j][k] *= inv * wv[k];
+        }
+    }
+    if (p.rope) {
+        // rotation partners: within the lane (adjacent pairs, even VPL), a fixed lane away (halves whose offset is a
+        // whole number of lanes), or through shared memory otherwise
+        const bool in_lane = p.rope == 2 && VPL % 2 == 0;
+        const bool by_shfl = p.rope == 1 && half % VPL == 0;
+        const int hl = int(half / VPL), src = lane < hl ? lane + hl : lane - hl;
+        // x' = x c - y s for the first of a pair, y' = y c + x s for the second (sn carries the sign)
+        if (in_lane) {
+#pragma unroll
+            for (int j = 0; j < NH; ++j)
+#pragma unroll
+                for (int k = 0; k < VPL; k += 2) {
+                    const float a = v[j][k], b = v[j][k + 1];
+                    v[j][k] = fmaf(a, cc[k], b * sn[k]);
+                    v[j][k + 1] = fmaf(b, cc[k + 1], a * sn[k + 1]);
+                }
+        } else if (by_shfl) {
+            // the partner of this lane's value k is value k of lane src, read before either is rewritten
+#pragma unroll
+            for (int j = 0; j < NH; ++j)
+#pragma unroll
+                for (int k = 0; k < VPL; ++k) {
+                    const float q = __shfl_sync(0xffffffffu, v[j][k], src);
+                    if (lane * VPL + k < p.rot)
+                        v[j][k] = fmaf(v[j][k], cc[k], q * sn[k]);
+                }
+        } else {
+#pragma unroll
+            for (int j = 0; j < NH; ++j) {
+                float* const hb = buf;
                 __syncwarp();
 #pragma unroll
                 for (int k = 0; k < VPL; ++k)
-                    buf[lane * VPL + k] = u[k];
+                    hb[lane * VPL + k] = v[j][k];
                 __syncwarp();
 #pragma unroll
                 for (int k = 0; k < VPL; ++k) {
                     const uint32_t i = lane * VPL + k;
                     const uint32_t pi = p.rope == 2 ? (i ^ 1) : (i < half ? i + half : i - half);
-                    q[k] = pi < p.dim ? buf[pi] : 0.0f;
+                    const float q = pi < p.dim ? hb[pi] : 0.0f;
+                    if (p.rope == 2 || i < p.rot)
+                        v[j][k] = fmaf(v[j][k], cc[k], q * sn[k]);
                 }
             }
+        }
+    }
 #pragma unroll
-            for (int k = 0; k < VPL; ++k) {
-                const uint32_t i = lane * VPL + k;
-                if (p.rope == 2 || i < p.rot)
-                    u[k] = fmaf(u[k], cc[k], q[k] * sn[k]);
+    for (int j = 0; j < NH; ++j)
+        if (uint32_t(j) < nh)
+            store16<VPL, T>(y0 + j * ystep, v[j]);
+}
+
+template <int VPL, typename T>
+__global__ void __launch_bounds__(HW * 32, VPL <= 4 ? 4 : 2) heads_kernel(const HeadsParams p)
+{
+    __shared__ float row_buf[HW][VPL * 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t r = blockIdx.x * HW + warp, h0 = blockIdx.y * HPW;
+    if (r >= p.rows)
+        return;
+    const uint32_t nh = min(uint32_t(HPW), p.heads - h0);
+    const int32_t t = p.map ? p.map[r] : int32_t(r);
+    float v[HPW][VPL];
+    float wv[VPL];
+    if (t >= 0) {
+        // all the warp's heads of this row in flight at once
+        const float* const x0 = p.x + uint64_t(t) * p.ld + p.col0 + uint64_t(h0) * p.stride + lane * VPL;
+#pragma unroll
+        for (int j = 0; j < HPW; ++j) {
+            if (uint32_t(j) < nh) {
+                if (VPL % 4 == 0 && p.vec4) {
+#pragma unroll
+                    for (int k = 0; k < VPL; k += 4) {
+                        const float4 w = __ldg(reinterpret_cast<const float4*>(x0 + j * p.stride + k));
+                        v[j][k] = w.x;
+                        v[j][k + 1] = w.y;
+                        v[j][k + 2] = w.z;
+                        v[j][k + 3] = w.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < VPL; ++k)
+                        v[j][k] = __ldg(x0 + j * p.stride + k);
+                }
             }
         }
-        store16<VPL, T>(y0 + j * ystep, u);
+        if (p.eps > 0.0f)
+#pragma unroll
+            for (int k = 0; k < VPL; ++k)
+                wv[k] = __ldg(p.w + lane * VPL + k);
     }
+    const float2* const cs = p.rope && t >= 0 ? reinterpret_cast<const float2*>(p.cs) + uint64_t(t) * p.cs_row : nullptr;
+    row_out<VPL, HPW, T>(p, t, r, h0, nh, v, wv, cs, row_buf[warp], lane);
 }
 
 template <typename T>

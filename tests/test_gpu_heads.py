@@ -205,3 +205,58 @@ def test_h3_sparse_block(ctx, oracle, dtype):
     ok, stats = C.within(got[:S], want[:S])
     assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
     assert np.all(got[S:] == 12345.0)
+
+
+BULK = [
+    # 16-byte aligned rows (128-bit loads).  A partial last block of rows, heads % 8 != 0, map holes, 96 of 128
+    # values rotated.
+    ("q-norm-rot96-map", dict(api="partial", dim=128, heads=11, stride=128, col0=4, rot=96, norm=True, T=203,
+                              n_pad=256, dtype=1, map=True)),
+    # heads not adjacent (stride 2 D), partial rotation
+    ("gated-q-rot64", dict(api="partial", dim=128, heads=9, stride=256, col0=0, rot=64, norm=True, T=77, n_pad=128,
+                           dtype=0, map=False)),
+    # adjacent-pair rotation with the norm (heads_norm)
+    ("pairs-norm", dict(api="norm", dim=128, heads=6, stride=128, col0=8, rot=128, norm=True, T=150, n_pad=192,
+                        dtype=1, map=False)),
+    # no rotation, no norm (v tiles), 64-wide heads; 96-wide heads rotated
+    ("v-d64", dict(api="partial", dim=64, heads=20, stride=64, col0=8, rot=0, norm=False, T=1000, n_pad=1024,
+                   dtype=1, map=False)),
+    ("k-d96", dict(api="partial", dim=96, heads=5, stride=96, col0=0, rot=96, norm=True, T=40, n_pad=64, dtype=0,
+                   map=True)),
+]
+
+
+@pytest.mark.parametrize("name,kw", BULK, ids=[n for n, _ in BULK])
+def test_heads_aligned_rows(ctx, oracle, name, kw):
+    import torch
+    rng = np.random.default_rng(hash(name) % 2 ** 32)
+    dim, H, stride, col0, rot, T, n_pad, dtype = (kw[k] for k in ("dim", "heads", "stride", "col0", "rot", "T",
+                                                                  "n_pad", "dtype"))
+    ld = col0 + stride * H + 12
+    assert ld % 4 == 0 and col0 % 4 == 0 and stride % 4 == 0
+    src_rows = T + 9
+    x = (rng.standard_normal((src_rows, ld)) * 2.0).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, dim).astype(np.float32) if kw["norm"] else None
+    m = None
+    if kw["map"]:
+        m = rng.permutation(src_rows)[:T].astype(np.int32)
+        m[::7] = -1
+    y = y_tile(H, n_pad, dim, dtype)
+    if kw["api"] == "norm":
+        cs = angles(rng, src_rows, 64)
+        ctx.heads_norm(tdev(x), ld, col0, H, T, n_pad, tdev(cs), 2, tdev(w), 1e-6, 0, y)
+        want = oracle.heads(x, ld, col0, 128, 128, 128, 2, T, H, n_pad, cs=cs, cs_row=64, w=w, eps=1e-6)
+    else:
+        cs = angles(rng, src_rows, max(rot // 2, 1))
+        ctx.heads_partial(tdev(x), ld, col0, stride, dim, rot, H, T, n_pad, tdev(cs) if rot else None,
+                          tdev(w) if w is not None else None, 1e-6, y, tdev(m) if m is not None else None)
+        want = oracle.heads(x, ld, col0, stride, dim, rot, 1 if rot else 0, T, H, n_pad, cs=cs, cs_row=rot // 2, w=w,
+                            eps=1e-6 if kw["norm"] else 0.0, map_=m)
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    got = bits(y)
+    far, exact = ulp_check(got[:, :T], want[:, :T], dtype)
+    assert far == 0 and exact >= 0.99, f"{far} elements beyond one ulp, {exact:.4f} bit-identical"
+    assert np.all(got[:, T:] == 0x7BFF), "rows past T are the caller's"
+    if m is not None:
+        assert np.all(got[:, :T][:, m < 0] == 0), "rows the map leaves empty are zero"
