@@ -65,7 +65,7 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[VPL])
 }
 
 // The rest of row r (model row t) once the values of its nh heads from h0 are in registers: RMS norm, rotation and
-// the 16-bit stores (zeros for t < 0).  cs: the row's angles (global or shared memory), wv: the norm weights of this
+// the 16-bit stores (zeros for t < 0).  cs: the row's angles, wv: the norm weights of this
 // lane's values, buf: dim floats of per-warp scratch, used when rotation partners cross lanes unevenly.
 template <int VPL, int NH, typename T>
 __device__ __forceinline__ void row_out(const HeadsParams& p, int32_t t, uint32_t r, uint32_t h0, uint32_t nh,
