@@ -11,7 +11,8 @@
  *     last failure.  Argument errors are reported before anything is enqueued (the reference throws
  *     std::runtime_error at the same points: src/models/runtime.cpp:266-267,290-291,311-312).
  * Element types: MAKO_F16 (IEEE half, the reference's `half` tiles) or MAKO_BF16.  Outputs are fp32 as in the
- * reference (o [n_q][width] floats, head h at column h * dim).
+ * reference (o [n_q][width] floats, head h at column h * dim), or the call's 16-bit type under
+ * MAKO_OPT_OUTPUT_16BIT.
  */
 #ifndef MAKO_ATTN_H
 #define MAKO_ATTN_H
@@ -47,7 +48,12 @@ enum {
     MAKO_OPT_DECODE_CHUNK = 3,
     /* 1: every call also records a CUDA event pair around its main kernel (the attention or split kernel, not the
      * bf16 V pre-pass, the decode combine or the group barriers) for mako_attn_kernel_times; 0 (default): none. */
-    MAKO_OPT_KERNEL_TIMING = 4
+    MAKO_OPT_KERNEL_TIMING = 4,
+    /* 1: mako_attention, mako_attention_decode, mako_attention_sparse and mako_attention_block_sparse write o in the
+     * call's 16-bit type (the values the reference's to_half / to_bf16 pass makes of its fp32 o before the output
+     * projection, src/gpu/runtime.cpp:164-190), 2 bytes per value, `o` pointing at that storage; o row widths of the
+     * prefill paths a multiple of 8.  0 (default): fp32 o.  The sharded forms keep fp32 (MAKO_ENOTSUP when set). */
+    MAKO_OPT_OUTPUT_16BIT = 5
 };
 
 typedef struct mako_attn_ctx mako_attn_ctx;

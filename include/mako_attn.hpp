@@ -30,6 +30,9 @@ public:
 
     void set_dtype(Dtype d) { dtype_ = int(d); }
     void set_stream(void* stream) { stream_ = stream; }
+    // o in the tiles' 16-bit type (what the reference's to_half / to_bf16 makes of o before the output projection)
+    // instead of fp32: `o` then points at that storage.
+    void set_output_16bit(bool on) { check(mako_attn_set_option(ctx_, MAKO_OPT_OUTPUT_16BIT, on ? 1 : 0)); }
 
     // TransformerRuntime::attention (src/models/runtime.hpp:90-95).
     void attention(const void* q, const void* k, const void* v, float* o, uint32_t n_q, uint32_t q_pad, uint32_t n_k,

@@ -256,10 +256,10 @@ __global__ void __launch_bounds__(NT) attn_mma_kernel(const AttnParams p)
             dst = p.map[row];
         if (dst < 0)
             continue;
-        float* orow = p.o + uint64_t(dst) * p.width + uint64_t(h) * D + 2 * tq;
+        const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * D + 2 * tq;
 #pragma unroll
         for (int nt = 0; nt < D / 8; ++nt)
-            *reinterpret_cast<float2*>(orow + nt * 8) = make_float2(acc[nt][2 * r] * inv[r], acc[nt][2 * r + 1] * inv[r]);
+            out_store2(p.o, orow + nt * 8, acc[nt][2 * r] * inv[r], acc[nt][2 * r + 1] * inv[r], p.o_type);
     }
 }
 

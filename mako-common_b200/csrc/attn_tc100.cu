@@ -46,6 +46,7 @@ struct __align__(64) TcParams {
     float* od[8];   // output destinations (this rank's o, then the peers' mapped o for the head-sharded form)
     uint32_t n_od;  // destinations in od
     uint32_t head0;  // column of local head h: (head0 + h) * 128
+    uint32_t o_type;  // element type of o (single destination): 0 fp32, 1 fp16, 2 bf16
     int* err;
     const float* vinv;  // per kv head: 1 / (the fp16 copy's scale), null for fp16 inputs
     uint32_t qk_fmt;    // Q / K element format: 0 fp16, 1 bf16
@@ -386,14 +387,8 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                 for (int i = 0; i < 32; ++i)
                     o[i] = 0u;
             }
-            if (grow < p.n_q) {
-                float* orow = p.od[0] + ooff;
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    *reinterpret_cast<float4*>(orow + c * 32 + i * 4) =
-                        make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                                    __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
-            }
+            if (grow < p.n_q)
+                out_store32(p.od[0], ooff + c * 32, o, inv, p.o_type);
         }
         }
     }
@@ -571,6 +566,9 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, const void* v16, cons
     p.err = err;
     p.vinv = bf ? vinv : nullptr;
     p.qk_fmt = bf ? 1u : 0u;
+    p.o_type = a.o_type;
+    if (p.n_od > 1 && p.o_type != 0)
+        return cudaErrorInvalidValue;  // the head-sharded epilogue stores fp32 boxes
     p.n_q = a.n_q;
     p.q_pad = a.q_pad;
     p.n_k = a.n_k;

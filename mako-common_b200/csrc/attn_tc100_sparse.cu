@@ -55,7 +55,7 @@ struct __align__(64) SpParams {
     const void* nsel;
     const uint8_t* valid;
     const int32_t* map;
-    uint32_t sel_i32, qk_fmt;
+    uint32_t sel_i32, qk_fmt, o_type;
     uint32_t n_q, q_pad, n_k, k_pad, heads, kv_heads, width, n_cubes, max_sel, dense0, dense1;
     uint32_t tiles_cube, tiles_total;
     float scale_log2;
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             store = dst >= 0;
         }
         const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
-        float* orow = p.o + uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * c;
+        const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * c;
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             uint32_t o[32];
@@ -490,13 +490,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 for (int e = 0; e < 32; ++e)
                     o[e] = 0u;
             }
-            if (store) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    *reinterpret_cast<float4*>(orow + 32 * k + e * 4) =
-                        make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
-                                    __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
-            }
+            if (store)
+                out_store32(p.o, orow + 32 * k, o, inv, p.o_type);
         }
     }
     __syncwarp();
@@ -558,6 +553,7 @@ cudaError_t launch_attn_tc_sparse(const AttnParams& a, int dtype, bool sel_i32, 
     p.map = a.map;
     p.sel_i32 = sel_i32 ? 1u : 0u;
     p.qk_fmt = bf ? 1u : 0u;
+    p.o_type = a.o_type;
     p.n_q = a.n_q;
     p.q_pad = a.q_pad;
     p.n_k = a.n_k;

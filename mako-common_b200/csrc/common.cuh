@@ -11,6 +11,58 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
 
+// ---- output element type (o_type: 0 fp32, 1 fp16, 2 bf16; the 16-bit types round to nearest even) ----------------
+
+__device__ __forceinline__ uint32_t out_pack2(float a, float b, uint32_t o_type)
+{
+    if (o_type == 1) {
+        __half2 v = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+// o[i] = v
+__device__ __forceinline__ void out_store1(void* o, uint64_t i, float v, uint32_t o_type)
+{
+    if (o_type == 0)
+        static_cast<float*>(o)[i] = v;
+    else if (o_type == 1)
+        static_cast<__half*>(o)[i] = __float2half_rn(v);
+    else
+        static_cast<__nv_bfloat16*>(o)[i] = __float2bfloat16_rn(v);
+}
+// o[i], o[i + 1] = a, b (i even)
+__device__ __forceinline__ void out_store2(void* o, uint64_t i, float a, float b, uint32_t o_type)
+{
+    if (o_type == 0)
+        *reinterpret_cast<float2*>(static_cast<float*>(o) + i) = make_float2(a, b);
+    else
+        *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(o) + i) = out_pack2(a, b, o_type);
+}
+// o[i .. i + 32) = r[0 .. 32) (fp32 bits) * s, i a multiple of 8 and o 16-byte aligned: 128-bit stores
+__device__ __forceinline__ void out_store32(void* o, uint64_t i, const uint32_t (&r)[32], float s, uint32_t o_type)
+{
+    if (o_type == 0) {
+        float* d = static_cast<float*>(o) + i;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            *reinterpret_cast<float4*>(d + 4 * e) =
+                make_float4(__uint_as_float(r[4 * e]) * s, __uint_as_float(r[4 * e + 1]) * s,
+                            __uint_as_float(r[4 * e + 2]) * s, __uint_as_float(r[4 * e + 3]) * s);
+        return;
+    }
+    uint16_t* d = static_cast<uint16_t*>(o) + i;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            w[k] = out_pack2(__uint_as_float(r[8 * e + 2 * k]) * s, __uint_as_float(r[8 * e + 2 * k + 1]) * s, o_type);
+        *reinterpret_cast<uint4*>(d + 8 * e) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 // 16 bytes global -> shared, zero-filled when !pred (nothing is read then).
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred)
 {

@@ -42,7 +42,7 @@ __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams
     if (start >= L) {
         if (L == 0 && split == 0 && !p.keep_partials)  // no key: the rows are 0
             for (uint32_t i = tid; i < nrows * D; i += DNT)
-                p.o[uint64_t(b) * p.o_bstride + uint64_t(h0 + i / D) * D + i % D] = 0.0f;
+                out_store1(p.o, uint64_t(b) * p.o_bstride + uint64_t(h0 + i / D) * D + i % D, 0.0f, p.o_type);
         return;
     }
     const uint32_t end = min(L, start + p.chunk);
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams
             O += so[(w * QR + r) * D + d] * fw;
         }
         if (ns == 1 && !p.keep_partials) {
-            p.o[uint64_t(b) * p.o_bstride + uint64_t(h0 + r) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
+            out_store1(p.o, uint64_t(b) * p.o_bstride + uint64_t(h0 + r) * D + d, Ls > 0.0f ? O / Ls : 0.0f, p.o_type);
         } else {
             const uint64_t row = (uint64_t(b) * p.heads + h0 + r) * p.n_splits + split;
             p.o_part[row * D + d] = O;
@@ -276,7 +276,7 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p)
     for (; s < ns; ++s)
         acc[0] += src[uint64_t(s) * D] * w[s];
     const float O = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-    p.o[uint64_t(b) * p.o_bstride + uint64_t(h) * D + d] = tot > 0.0f ? O / tot : 0.0f;
+    out_store1(p.o, uint64_t(b) * p.o_bstride + uint64_t(h) * D + d, tot > 0.0f ? O / tot : 0.0f, p.o_type);
 }
 
 template <int D, typename T>

@@ -32,6 +32,7 @@ struct AttnParams {
     // the single destination `o` at column h * dim.
     float* od[8];
     uint32_t n_od, head0;
+    uint32_t o_type;  // element type of o: 0 fp32, 1 fp16, 2 bf16 (single-destination forms)
 };
 
 // Portable flash attention on mma.sync tensor cores, any head width of 64 / 128 / 256.
@@ -64,6 +65,7 @@ struct DecodeParams {
     uint32_t batch, heads, kv_heads, chunk, n_splits;
     float scale;
     uint32_t keep_partials;  // 1: always write partials (the KV-sharded combine reads them), never o
+    uint32_t o_type;         // element type of o: 0 fp32, 1 fp16, 2 bf16
 };
 // Keys a split takes and how many splits, for the longest sequence max_len (chunk_opt: 0 automatic, else the
 // requested multiple of 64).

@@ -25,6 +25,7 @@ struct mako_attn_ctx {
     uint32_t decode_chunk = 0;  // MAKO_OPT_DECODE_CHUNK
     uint64_t launches = 0;   // kernels enqueued
     bool timing = false;     // MAKO_OPT_KERNEL_TIMING
+    bool out16 = false;      // MAKO_OPT_OUTPUT_16BIT
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;  // main-kernel event pairs, [0, used) recorded
     size_t used = 0;
     struct Buf {
@@ -66,6 +67,8 @@ int cuda_fail(const char* what, cudaError_t e)
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+// Element type of o for a call of `dtype`: 0 fp32, else the call's 16-bit type (MAKO_OPT_OUTPUT_16BIT).
+uint32_t out_type(const mako_attn_ctx* ctx, int dtype) { return ctx->out16 ? (dtype == MAKO_BF16 ? 2u : 1u) : 0u; }
 
 // Runs the calls of one entry point with the context's device current, the caller's device restored after.
 struct DeviceGuard {
@@ -237,6 +240,9 @@ int mako_attn_set_option(mako_attn_ctx* ctx, int option, int64_t value)
     case MAKO_OPT_KERNEL_TIMING:
         ctx->timing = value != 0;
         return MAKO_OK;
+    case MAKO_OPT_OUTPUT_16BIT:
+        ctx->out16 = value != 0;
+        return MAKO_OK;
     case MAKO_OPT_DECODE_CHUNK:
         if (value < 0 || value % 64 || value > (int64_t(1) << 30))
             return fail(MAKO_EINVAL, "decode chunk %lld (0 or a multiple of 64)", (long long)value);
@@ -313,6 +319,9 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
         return fail(MAKO_EINVAL, "attention: o rows of %u floats for %u heads of %u", width, heads, dim);
     if (!q || !k || !v || !o || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
         return fail(MAKO_EINVAL, "attention: null or unaligned tensor (16-byte alignment)");
+    // the prefill kernels store o rows 16 bytes at a time: rows keep o's alignment
+    if (!(n_q == 1 && ctx->decode_route) && width % (ctx->out16 ? 8 : 4))
+        return fail(MAKO_EINVAL, "attention: o row width %u (a multiple of %d)", width, ctx->out16 ? 8 : 4);
     if (n_q == 0)
         return MAKO_OK;
     DeviceGuard dg(ctx->device);
@@ -334,6 +343,7 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
         p.k_bstride = 0;
         p.k_hstride = uint64_t(k_pad) * dim;
         p.o_bstride = width;
+        p.o_type = out_type(ctx, dtype);
         p.batch = 1;
         p.heads = heads;
         p.kv_heads = kv_heads;
@@ -368,6 +378,7 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
     p.q_pos0 = q_pos0;
     p.block = block;
     p.width = width;
+    p.o_type = out_type(ctx, dtype);
     p.scale = 1.0f / sqrtf(float(dim));
     const bool tc_ok = dim == 128 && ctx->cc_major == 10;
     if (ctx->prefill_kernel == 2 && !tc_ok)
@@ -432,6 +443,7 @@ int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const voi
     p.k_hstride = uint64_t(k_stride) * dim;
     p.k_bstride = uint64_t(kv_heads) * p.k_hstride;
     p.o_bstride = uint64_t(heads) * dim;
+    p.o_type = out_type(ctx, dtype);
     p.batch = batch;
     p.heads = heads;
     p.kv_heads = kv_heads;
@@ -508,10 +520,13 @@ namespace {
 
 int sparse_common(mako_attn_ctx* ctx, void* stream, int dtype, mako::AttnParams& p, bool sel_i32)
 {
+    if (p.width % (ctx->out16 ? 8 : 4))  // o rows are stored 16 bytes at a time
+        return fail(MAKO_EINVAL, "attention_sparse: o row width %u (a multiple of %d)", p.width, ctx->out16 ? 8 : 4);
     DeviceGuard dg(ctx->device);
     if (dg.err != cudaSuccess)
         return cuda_fail("set device", dg.err);
     p.scale = 1.0f / sqrtf(128.0f);
+    p.o_type = out_type(ctx, dtype);
     auto st = static_cast<cudaStream_t>(stream);
     const bool tc_ok = ctx->cc_major == 10;
     if (ctx->prefill_kernel == 2 && !tc_ok)
@@ -1019,6 +1034,10 @@ int mako_attention_gather(mako_attn_group* g, void* stream, int dtype, const voi
     mako_attn_ctx* ctx = g->ctx;
     if (ctx->cc_major != 10)
         return fail(MAKO_ENOTSUP, "attention_gather: the tcgen05 kernel needs sm_100 (sm_%d)", ctx->cc_major * 10);
+    if (ctx->out16)
+        return fail(MAKO_ENOTSUP, "attention_gather: o is fp32 in the sharded forms (MAKO_OPT_OUTPUT_16BIT is set)");
+    if (width % 4)
+        return fail(MAKO_EINVAL, "attention_gather: o row width %u (a multiple of 4)", width);
     if (!heads || !kv_heads || heads % kv_heads)
         return fail(MAKO_EINVAL, "attention_gather: %u heads over %u kv heads", heads, kv_heads);
     if (q_pad % 64 || q_pad < n_q || k_pad < n_k)
@@ -1092,6 +1111,8 @@ int mako_attention_decode_kv_sharded(mako_attn_group* g, void* stream, int dtype
     if (int rc = check_group(g, dtype))
         return rc;
     mako_attn_ctx* ctx = g->ctx;
+    if (ctx->out16)
+        return fail(MAKO_ENOTSUP, "decode_kv_sharded: o is fp32 in the sharded forms (MAKO_OPT_OUTPUT_16BIT is set)");
     if (dim != 64 && dim != 128 && dim != 256)
         return fail(MAKO_EINVAL, "decode_kv_sharded: heads of %u", dim);
     if (!heads || !kv_heads || heads % kv_heads)
