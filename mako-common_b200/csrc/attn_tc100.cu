@@ -1,5 +1,5 @@
-// Flash attention for 128-wide heads on sm_100a tensor cores (tcgen05 UMMA, TMEM accumulators, TMA-fed shared
-// memory): the dense masked form of TransformerRuntime::attention (src/models/runtime.cpp:262-273; maths of
+// Flash attention for 64- and 128-wide heads on sm_100a tensor cores (tcgen05 UMMA, TMEM accumulators, TMA-fed
+// shared memory): the dense masked form of TransformerRuntime::attention (src/models/runtime.cpp:262-273; maths of
 // flash_attn_coop, src/kernels/ops.metal:230-363).
 //
 // A CTA owns 256 query rows of one head as two 128-row tiles A and B that share every K / V tile (half the K / V
@@ -32,12 +32,15 @@ namespace {
 
 using namespace tc;
 
-constexpr int TD = 128, TBM = 128, TBN = 128, TNS = 2, TNT = 384;
-constexpr uint32_t BOX_BYTES = 128 * 64 * 2;   // one TMA box: 128 rows x 64 16-bit values
-constexpr uint32_t TILE_BYTES = 2 * BOX_BYTES;  // 128 rows x 128 values
-constexpr uint32_t SMEM_Q = 0, SMEM_K = 2 * TILE_BYTES, SMEM_V = SMEM_K + TNS * TILE_BYTES;
-constexpr uint32_t SMEM_BAR = SMEM_V + TNS * TILE_BYTES;
-constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 256 + 1024;  // + barriers + alignment slack
+constexpr int TBM = 128, TBN = 128, TNS = 2, TNT = 384;
+constexpr uint32_t BOX_BYTES = 128 * 64 * 2;  // one TMA box: 128 rows x 64 16-bit values
+// Shared memory for TD-wide heads (64 or 128): Q of both tiles, the K and V rings, the barriers.
+template <int TD>
+struct TcSmem {
+    static constexpr uint32_t TILE = (TD / 64) * BOX_BYTES;  // 128 rows x TD values
+    static constexpr uint32_t Q = 0, K = 2 * TILE, V = K + TNS * TILE, BAR = V + TNS * TILE;
+    static constexpr uint32_t TOTAL = BAR + 256 + 1024;  // + barriers + alignment slack
+};
 constexpr long long WAIT_LIMIT = 1ll << 31;             // clock cycles (~1 s) before a wait gives up
 
 struct __align__(64) TcParams {
@@ -60,14 +63,17 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// GATHER: the head-sharded form's epilogue (TMA stores into every rank's o); otherwise plain stores into p.od[0].
-template <bool GATHER>
+// TD: head width (64 or 128).  GATHER: the head-sharded form's epilogue (TMA stores into every rank's o, 128-wide
+// heads); otherwise plain stores into p.od[0].
+template <int TD, bool GATHER>
 __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__ TcParams p)
 {
+    constexpr uint32_t TILE_BYTES = TcSmem<TD>::TILE;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
-    const uint32_t sQ = base + SMEM_Q, sK = base + SMEM_K, sV = base + SMEM_V, sB = base + SMEM_BAR;
+    const uint32_t sQ = base + TcSmem<TD>::Q, sK = base + TcSmem<TD>::K, sV = base + TcSmem<TD>::V;
+    const uint32_t sB = base + TcSmem<TD>::BAR;
     // barriers
     const uint32_t q_full = sB;
     auto k_full = [&](uint32_t s) { return sB + 8 + 8 * s; };
@@ -125,7 +131,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             bool ok = true;
             mbar_expect_tx(q_full, 2 * TILE_BYTES);
             for (int x = 0; x < 2; ++x)
-                for (int half = 0; half < 2; ++half)
+                for (int half = 0; half < TD / 64; ++half)
                     tma_load_3d(sQ + x * TILE_BYTES + half * BOX_BYTES, &p.tq, q_full, half * 64, q0 + x * TBM, h);
             uint32_t issued = 0;
             for (uint32_t j = 0; j < nb && ok; ++j) {
@@ -135,7 +141,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                     break;
                 }
                 mbar_expect_tx(k_full(s), TILE_BYTES);
-                for (int half = 0; half < 2; ++half)
+                for (int half = 0; half < TD / 64; ++half)
                     tma_load_3d(sK + s * TILE_BYTES + half * BOX_BYTES, &p.tk, k_full(s), half * 64, j * TBN, kvh);
                 if (j >= TNS && !mbar_wait(v_empty(s), ph ^ 1, WAIT_LIMIT)) {
                     ok = false;
@@ -143,7 +149,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                     break;
                 }
                 mbar_expect_tx(v_full(s), TILE_BYTES);
-                for (int half = 0; half < 2; ++half)
+                for (int half = 0; half < TD / 64; ++half)
                     tma_load_3d(sV + s * TILE_BYTES + half * BOX_BYTES, &p.tv, v_full(s), half * 64, j * TBN, kvh);
                 issued = 2 * (j + 1);
             }
@@ -310,7 +316,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             if (__any_sync(0xffffffffu, resc && j > 0)) {
                 const float g = resc ? f : 1.0f;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < TD / 32; ++c) {
                     uint32_t o[32];
                     tmem_ld32(tl + colO + c * 32, o);
                     tmem_wait_ld();
@@ -339,7 +345,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             // asynchronously -- the next CTA on this SM computes while they cross NVLink.  Two halves of 64 columns.
             const uint32_t stage = sQ + x * TILE_BYTES;
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
+            for (int half = 0; half < TD / 64; ++half) {
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
                     uint32_t o[32];
@@ -376,7 +382,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
         } else {
         const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(h) * TD;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < TD / 32; ++c) {
             uint32_t o[32];
             if (ok && nb > 0) {
                 tmem_ld32(tl + colO + c * 32, o);
@@ -404,15 +410,15 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
 // ---- bf16 V -> scaled fp16 copy -----------------------------------------------------------------------------------
 
 // vmax[kvh] = max |v| over the rows that can be attended (rows < n_rows with valid[row] != 0), as float bits.
-__global__ void __launch_bounds__(256) vmax_kernel(const __nv_bfloat16* v, uint32_t* vmax, uint32_t k_pad,
+__global__ void __launch_bounds__(256) vmax_kernel(const __nv_bfloat16* v, uint32_t* vmax, uint32_t dim, uint32_t k_pad,
                                                    uint32_t n_rows, const uint8_t* valid)
 {
     const uint32_t kvh = blockIdx.y;
-    const uint4* src = reinterpret_cast<const uint4*>(v + uint64_t(kvh) * k_pad * TD);
-    const uint64_t chunks = uint64_t(n_rows) * (TD / 8);
+    const uint4* src = reinterpret_cast<const uint4*>(v + uint64_t(kvh) * k_pad * dim);
+    const uint64_t chunks = uint64_t(n_rows) * (dim / 8);
     uint32_t best = 0;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < chunks; i += uint64_t(gridDim.x) * blockDim.x) {
-        if (valid && !valid[i / (TD / 8)])
+        if (valid && !valid[i / (dim / 8)])
             continue;
         const uint4 w = src[i];
         const uint32_t words[4] = {w.x, w.y, w.z, w.w};
@@ -443,7 +449,7 @@ __device__ __forceinline__ void v_scale(uint32_t bits, float& s, float& inv)
 }
 
 __global__ void __launch_bounds__(256) vconv_kernel(const __nv_bfloat16* v, __half* v16, const uint32_t* vmax,
-                                                    float* vinv, uint32_t k_pad, uint32_t n_rows,
+                                                    float* vinv, uint32_t dim, uint32_t k_pad, uint32_t n_rows,
                                                     const uint8_t* valid)
 {
     const uint32_t kvh = blockIdx.y;
@@ -451,11 +457,11 @@ __global__ void __launch_bounds__(256) vconv_kernel(const __nv_bfloat16* v, __ha
     v_scale(vmax[kvh], s, inv);
     if (blockIdx.x == 0 && threadIdx.x == 0)
         vinv[kvh] = inv;
-    const uint4* src = reinterpret_cast<const uint4*>(v + uint64_t(kvh) * k_pad * TD);
-    uint4* dst = reinterpret_cast<uint4*>(v16 + uint64_t(kvh) * k_pad * TD);
-    const uint64_t chunks = uint64_t(k_pad) * (TD / 8);
+    const uint4* src = reinterpret_cast<const uint4*>(v + uint64_t(kvh) * k_pad * dim);
+    uint4* dst = reinterpret_cast<uint4*>(v16 + uint64_t(kvh) * k_pad * dim);
+    const uint64_t chunks = uint64_t(k_pad) * (dim / 8);
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < chunks; i += uint64_t(gridDim.x) * blockDim.x) {
-        const uint32_t row = uint32_t(i / (TD / 8));
+        const uint32_t row = uint32_t(i / (dim / 8));
         uint4 out = make_uint4(0, 0, 0, 0);
         if (row < n_rows && (!valid || valid[row])) {
             const uint4 w = src[i];
@@ -487,14 +493,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
-// [heads][rows][128] 16-bit tiles, boxes of 128 rows x 64 values, 128-byte swizzle, zero fill past `rows`.
-bool head_map(CUtensorMap* map, const void* ptr, bool bf16, uint32_t rows, uint32_t heads)
+// [heads][rows][dim] 16-bit tiles, boxes of 128 rows x 64 values, 128-byte swizzle, zero fill past `rows`.
+bool head_map(CUtensorMap* map, const void* ptr, bool bf16, uint32_t dim, uint32_t rows, uint32_t heads)
 {
     auto enc = encode_fn();
     if (!enc)
         return false;
-    cuuint64_t dims[3] = {TD, rows, heads};
-    cuuint64_t strides[2] = {uint64_t(TD) * 2, uint64_t(rows) * TD * 2};
+    cuuint64_t dims[3] = {dim, rows, heads};
+    cuuint64_t strides[2] = {uint64_t(dim) * 2, uint64_t(rows) * dim * 2};
     cuuint32_t box[3] = {64, 128, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
@@ -520,33 +526,36 @@ bool out_map(CUtensorMap* map, float* o, uint32_t n_q, uint32_t width)
 
 } // namespace
 
-cudaError_t launch_v_to_f16(const void* v, void* v16, uint32_t* vmax, float* vinv, uint32_t kv_heads, uint32_t k_pad,
-                            uint32_t n_rows, const uint8_t* valid, int num_sms, cudaStream_t st)
+cudaError_t launch_v_to_f16(const void* v, void* v16, uint32_t* vmax, float* vinv, uint32_t dim, uint32_t kv_heads,
+                            uint32_t k_pad, uint32_t n_rows, const uint8_t* valid, int num_sms, cudaStream_t st)
 {
     cudaError_t e = cudaMemsetAsync(vmax, 0, kv_heads * sizeof(uint32_t), st);
     if (e != cudaSuccess)
         return e;
-    const uint64_t chunks = uint64_t(k_pad) * (TD / 8);
+    const uint64_t chunks = uint64_t(k_pad) * (dim / 8);
     uint32_t bx = uint32_t((chunks + 255) / 256);
     const uint32_t cap = uint32_t((num_sms * 8 + kv_heads - 1) / kv_heads);
     bx = bx < 1 ? 1 : (bx > cap ? cap : bx);
-    vmax_kernel<<<dim3(bx, kv_heads), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(v), vmax, k_pad, n_rows, valid);
+    vmax_kernel<<<dim3(bx, kv_heads), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(v), vmax, dim, k_pad, n_rows,
+                                                     valid);
     if ((e = cudaGetLastError()) != cudaSuccess)
         return e;
     vconv_kernel<<<dim3(bx, kv_heads), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(v), static_cast<__half*>(v16),
-                                                      vmax, vinv, k_pad, n_rows, valid);
+                                                      vmax, vinv, dim, k_pad, n_rows, valid);
     return cudaGetLastError();
 }
 
-cudaError_t launch_attn_tc(const AttnParams& a, int dtype, const void* v16, const float* vinv, int* err,
+cudaError_t launch_attn_tc(const AttnParams& a, int dtype, int dim, const void* v16, const float* vinv, int* err,
                            cudaStream_t st)
 {
     if (a.n_q == 0 || a.heads == 0)
         return cudaSuccess;
+    if (dim != 64 && dim != 128)
+        return cudaErrorInvalidValue;
     TcParams p;
     const bool bf = dtype == kBF16;
-    if (!head_map(&p.tq, a.q, bf, a.q_pad, a.heads) || !head_map(&p.tk, a.k, bf, a.k_pad, a.kv_heads) ||
-        !head_map(&p.tv, bf ? v16 : a.v, false, a.k_pad, a.kv_heads))
+    if (!head_map(&p.tq, a.q, bf, dim, a.q_pad, a.heads) || !head_map(&p.tk, a.k, bf, dim, a.k_pad, a.kv_heads) ||
+        !head_map(&p.tv, bf ? v16 : a.v, false, dim, a.k_pad, a.kv_heads))
         return cudaErrorInvalidValue;
     if (a.n_od == 0) {
         p.od[0] = a.o;
@@ -581,11 +590,14 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, const void* v16, cons
     p.n_tiles = (a.q_pad + 2 * TBM - 1) / (2 * TBM);
     p.scale_log2 = a.scale * kLog2e;
     const bool gather = p.n_od > 1;
-    auto kern = gather ? attn_tc_kernel<true> : attn_tc_kernel<false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL);
+    if (gather && dim != 128)
+        return cudaErrorInvalidValue;  // the head-sharded epilogue stages 128-wide rows in the Q buffer
+    auto kern = dim == 64 ? attn_tc_kernel<64, false> : gather ? attn_tc_kernel<128, true> : attn_tc_kernel<128, false>;
+    const uint32_t smem = dim == 64 ? TcSmem<64>::TOTAL : TcSmem<128>::TOTAL;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess)
         return e;
-    kern<<<dim3(p.n_tiles, a.heads), TNT, SMEM_TOTAL, st>>>(p);
+    kern<<<dim3(p.n_tiles, a.heads), TNT, smem, st>>>(p);
     return cudaGetLastError();
 }
 

@@ -38,18 +38,19 @@ struct AttnParams {
 // Portable flash attention on mma.sync tensor cores, any head width of 64 / 128 / 256.
 cudaError_t launch_attn_mma(const AttnParams& p, int dtype, int dim, bool sparse, bool sel_i32, cudaStream_t s);
 
-// Flash attention for 128-wide heads on sm_100a (tcgen05 / TMEM / TMA).  bf16 inputs need v16 / vinv from
-// launch_v_to_f16; err receives a nonzero code if a pipeline wait timed out.
-cudaError_t launch_attn_tc(const AttnParams& p, int dtype, const void* v16, const float* vinv, int* err,
+// Flash attention for 64- or 128-wide heads (dim) on sm_100a (tcgen05 / TMEM / TMA); the head-sharded form (n_od > 1)
+// for 128-wide heads.  bf16 inputs need v16 / vinv from launch_v_to_f16; err receives a nonzero code if a pipeline
+// wait timed out.
+cudaError_t launch_attn_tc(const AttnParams& p, int dtype, int dim, const void* v16, const float* vinv, int* err,
                            cudaStream_t s);
 // Block-sparse attention for 128-wide heads on sm_100a: two query cubes per 128-row UMMA tile, their key-cube lists
 // walked in lockstep.  bf16 inputs need v16 / vinv (launch_v_to_f16 over all k_pad rows with the valid mask).
 cudaError_t launch_attn_tc_sparse(const AttnParams& p, int dtype, bool sel_i32, const void* v16, const float* vinv,
                                   int* err, cudaStream_t s);
 // v16 = fp16(v * 2^k) per kv head (k puts the head's max |v| over rows < n_rows with valid[row] in [2^14, 2^15);
-// other rows 0) and vinv = 2^-k.  vmax: [kv_heads] scratch.
-cudaError_t launch_v_to_f16(const void* v, void* v16, uint32_t* vmax, float* vinv, uint32_t kv_heads, uint32_t k_pad,
-                            uint32_t n_rows, const uint8_t* valid, int num_sms, cudaStream_t s);
+// other rows 0) and vinv = 2^-k, for [kv_heads][k_pad][dim] tiles.  vmax: [kv_heads] scratch.
+cudaError_t launch_v_to_f16(const void* v, void* v16, uint32_t* vmax, float* vinv, uint32_t dim, uint32_t kv_heads,
+                            uint32_t k_pad, uint32_t n_rows, const uint8_t* valid, int num_sms, cudaStream_t s);
 
 // Split-KV decode: one query row per (sequence, head) over keys [0, len).
 struct DecodeParams {

@@ -380,10 +380,10 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
     p.width = width;
     p.o_type = out_type(ctx, dtype);
     p.scale = 1.0f / sqrtf(float(dim));
-    const bool tc_ok = dim == 128 && ctx->cc_major == 10;
+    const bool tc_ok = (dim == 64 || dim == 128) && ctx->cc_major == 10;
     if (ctx->prefill_kernel == 2 && !tc_ok)
-        return fail(MAKO_ENOTSUP, "attention: the tcgen05 kernel takes 128-wide heads on sm_100 (got %u, sm_%d)", dim,
-                    ctx->cc_major * 10);
+        return fail(MAKO_ENOTSUP, "attention: the tcgen05 kernel takes 64- or 128-wide heads on sm_100 (got %u, sm_%d)",
+                    dim, ctx->cc_major * 10);
     if (tc_ok && ctx->prefill_kernel != 1) {
         void *v16 = nullptr, *vmax = nullptr, *vinv = nullptr;
         if (dtype == MAKO_BF16) {
@@ -394,14 +394,14 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
             if (int rc = scratch(ctx, "vinv", size_t(kv_heads) * 4, &vinv))
                 return rc;
             cudaError_t e = mako::launch_v_to_f16(v, v16, static_cast<uint32_t*>(vmax), static_cast<float*>(vinv),
-                                                  kv_heads, k_pad, n_k, nullptr, ctx->num_sms, st);
+                                                  dim, kv_heads, k_pad, n_k, nullptr, ctx->num_sms, st);
             if (e != cudaSuccess)
                 return cuda_fail("attention (V to fp16)", e);
             ctx->launches += 2;
         }
         ctx->launches += 1;
         KernelTimer t(ctx, st);
-        cudaError_t e = mako::launch_attn_tc(p, dtype, v16, static_cast<const float*>(vinv), ctx->err, st);
+        cudaError_t e = mako::launch_attn_tc(p, dtype, int(dim), v16, static_cast<const float*>(vinv), ctx->err, st);
         t.stop();
         return launched("attention (tcgen05)", e);
     }
@@ -541,7 +541,7 @@ int sparse_common(mako_attn_ctx* ctx, void* stream, int dtype, mako::AttnParams&
             if (int rc = scratch(ctx, "vinv", size_t(p.kv_heads) * 4, &vinv))
                 return rc;
             cudaError_t e = mako::launch_v_to_f16(p.v, v16, static_cast<uint32_t*>(vmax), static_cast<float*>(vinv),
-                                                  p.kv_heads, p.k_pad, p.k_pad, p.valid, ctx->num_sms, st);
+                                                  128, p.kv_heads, p.k_pad, p.k_pad, p.valid, ctx->num_sms, st);
             if (e != cudaSuccess)
                 return cuda_fail("attention_sparse (V to fp16)", e);
             ctx->launches += 2;
@@ -1083,7 +1083,7 @@ int mako_attention_gather(mako_attn_group* g, void* stream, int dtype, const voi
         if (int rc = scratch(ctx, "vinv", size_t(kv_heads) * 4, &vinv))
             return rc;
         cudaError_t e = mako::launch_v_to_f16(v, v16, static_cast<uint32_t*>(vmax), static_cast<float*>(vinv),
-                                              kv_heads, k_pad, n_k, nullptr, ctx->num_sms, st);
+                                              128, kv_heads, k_pad, n_k, nullptr, ctx->num_sms, st);
         if (e != cudaSuccess)
             return cuda_fail("attention_gather (V to fp16)", e);
         ctx->launches += 2;
@@ -1094,7 +1094,7 @@ int mako_attention_gather(mako_attn_group* g, void* stream, int dtype, const voi
         return cuda_fail("attention_gather (enter barrier)", e);
     if (n_q) {
         KernelTimer t(ctx, st);
-        e = mako::launch_attn_tc(p, dtype, v16, static_cast<const float*>(vinv), ctx->err, st);
+        e = mako::launch_attn_tc(p, dtype, 128, v16, static_cast<const float*>(vinv), ctx->err, st);
         t.stop();
         if (e != cudaSuccess)
             return cuda_fail("attention_gather (tcgen05)", e);

@@ -48,22 +48,24 @@ def both(ctx, call, o32, o16, dtype):
 
 
 
+@pytest.mark.parametrize("dim", [64, 128])
 @pytest.mark.parametrize("kernel", [0, 1], ids=["auto", "mma"])
 @pytest.mark.parametrize("dtype", [0, 1])
-def test_dense_out16(ctx, kernel, dtype):
+def test_dense_out16(ctx, kernel, dtype, dim):
     import mako_attn
-    case = C.dense_case(seed=60 + dtype, heads=4, kv_heads=2, dim=128, n_q=300, n_k=300, dtype=dtype)
+    case = C.dense_case(seed=60 + dtype, heads=4, kv_heads=2, dim=dim, n_q=300, n_k=300, dtype=dtype)
     q, k, v = dev(case["q"], dtype), dev(case["k"], dtype), dev(case["v"], dtype)
-    width = 4 * 128 + 8  # a wider o row: the columns past the heads stay untouched
+    hw = 4 * dim
+    width = hw + 8  # a wider o row: the columns past the heads stay untouched
     o32, o16 = out_pair(300 + 2, width, dtype)
     ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, kernel)
     try:
         f32, b16 = both(ctx, lambda o: ctx.attention(q, k, v, o, 300, case["q_pad"], 300, case["k_pad"], 4, 2, 0,
-                                                     0xFFFFFFFF, 128, width), o32, o16, dtype)
+                                                     0xFFFFFFFF, dim, width), o32, o16, dtype)
     finally:
         ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 0)
-    np.testing.assert_array_equal(b16[:300, :512], round16(f32[:300, :512], dtype))
-    assert np.all(b16[:300, 512:] == SENT16) and np.all(b16[300:] == SENT16)
+    np.testing.assert_array_equal(b16[:300, :hw], round16(f32[:300, :hw], dtype))
+    assert np.all(b16[:300, hw:] == SENT16) and np.all(b16[300:] == SENT16)
 
 
 @pytest.mark.parametrize("dim", [64, 128, 256])

@@ -54,6 +54,9 @@ DENSE = [
     ("q-offset", dict(seed=4, heads=4, kv_heads=1, dim=128, n_q=70, n_k=600, q_pos0=530, dtype=0)),
     ("d64", dict(seed=5, heads=6, kv_heads=3, dim=64, n_q=257, n_k=257, dtype=0)),
     ("d64-bidir-bf16", dict(seed=6, heads=2, kv_heads=2, dim=64, n_q=130, n_k=130, block=0, dtype=1)),
+    ("d64-gqa-long", dict(seed=11, heads=8, kv_heads=2, dim=64, n_q=1100, n_k=1100, dtype=1)),
+    ("d64-offset-block", dict(seed=12, heads=4, kv_heads=4, dim=64, n_q=300, n_k=700, q_pos0=400, block=500,
+                              dtype=0)),
     ("d256", dict(seed=7, heads=4, kv_heads=2, dim=256, n_q=190, n_k=190, dtype=0)),
     ("d256-bf16", dict(seed=8, heads=2, kv_heads=1, dim=256, n_q=64, n_k=300, block=0, dtype=1)),
     ("video-rms", dict(seed=9, heads=2, kv_heads=2, dim=128, n_q=1000, n_k=1000, block=0, dtype=1, qk_rms_norm=True)),
@@ -64,9 +67,9 @@ DENSE = [
 @pytest.mark.parametrize("name,kw", DENSE, ids=[n for n, _ in DENSE])
 @pytest.mark.parametrize("kernel", [0, 1, 2], ids=["auto", "mma", "tcgen05"])
 def test_dense(ctx, oracle, name, kw, kernel):
-    """kernel 0: the default choice (tcgen05 for 128-wide heads), 1: the portable mma.sync kernel, 2: tcgen05."""
-    if kernel == 2 and kw["dim"] != 128:
-        pytest.skip("the tcgen05 kernel takes 128-wide heads")
+    """kernel 0: the default choice (tcgen05 for 64- and 128-wide heads), 1: the portable mma.sync kernel, 2: tcgen05."""
+    if kernel == 2 and kw["dim"] == 256:
+        pytest.skip("the tcgen05 kernel takes 64- and 128-wide heads")
     case = C.dense_case(**kw)
     got = run_dense(ctx, case, kernel)
     assert ctx.device_error() == 0
@@ -346,12 +349,12 @@ def test_sparse_h3_layout(ctx, oracle, kernel, dtype):
 def test_tcgen05_rejects_other_widths(ctx):
     import torch
     import mako_attn
-    q = torch.zeros(64 * 64, dtype=torch.float16, device="cuda")
-    o = torch.zeros(64 * 64, dtype=torch.float32, device="cuda")
+    q = torch.zeros(64 * 256, dtype=torch.float16, device="cuda")
+    o = torch.zeros(64 * 256, dtype=torch.float32, device="cuda")
     ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 2)
     try:
         with pytest.raises(mako_attn.MakoError, match="tcgen05"):
-            ctx.attention(q, q, q, o, 10, 64, 10, 64, 1, 1, 0, 0, 64)
+            ctx.attention(q, q, q, o, 10, 64, 10, 64, 1, 1, 0, 0, 256)
     finally:
         ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 0)
 
