@@ -1,0 +1,386 @@
+// Flash attention for 256-wide heads on sm_100a tensor cores: the dense masked form of TransformerRuntime::attention
+// (src/models/runtime.cpp:262-273) for the 256-wide heads of Qwen3.5's gated attention layers
+// (src/models/qwen_text.cpp:397-422, flash_attn_sg<256, ...> in the reference, src/kernels/ops.metal:106-214).
+//
+// A 128-row Q tile of 256-wide heads is 64 KB of shared memory, so a CTA holds one tile and walks the keys in 64-row
+// tiles (K and V 32 KB each, two-stage rings): 192 KB in all.  Q.K^T is M 128 x N 64 x K 256 (16 instructions of
+// K 16 at N 64, about two thirds of the full rate), P.V is M 128 x N 256 x K 64 (4 instructions, full rate).
+//
+// Warp roles (384 threads): warp 0 loads Q once and the K ring, warp 2 the V ring (TMA, 128-byte swizzle, boxes of
+// 64 values), warp 1's elected thread issues UMMA in the fixed order QK(0), QK(1), then per key tile PV(j),
+// QK(j + 2), with a commit after each group for the consumer and one releasing the ring stage it read.  Warps 4-11
+// run the softmax: query row r (TMEM lane r) belongs to one thread of warps 4-7 (scores 0-31 of a key tile) and one
+// of warps 8-11 (scores 32-63), which agree on the row maximum through shared memory.
+// TMEM: S in two buffers (0-63, 64-127), P in two buffers (128-159, 160-191, fp16 pairs, the A operand of P.V) and O
+// (256-511).  QK(j + 2) waits only until the softmax has read S(j); the softmax writes P(j) into the other buffer
+// from P.V(j - 1), so it never waits for a product except to rescale O (rare, the reference's lazy rescale).
+//
+// Precision as the 128-wide kernel (attn_tc100.cu): Q.K^T in the input type, P.V in fp16 (bf16 V through the scaled
+// fp16 copy), fp32 accumulation; every wait is bounded and a timeout sets p.err.
+#include "common.cuh"
+#include "kernels.h"
+#include "tc100.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace mako {
+namespace {
+
+using namespace tc;
+
+constexpr int WD = 256, WBM = 128, WBN = 64, WNT = 384;
+constexpr uint32_t QBOX = 128 * 64 * 2;              // Q: 128 rows x 64 values
+constexpr uint32_t KBOX = 64 * 64 * 2;               // K / V: 64 rows x 64 values
+constexpr uint32_t QTILE = 4 * QBOX, KTILE = 4 * KBOX;  // 64 KB, 32 KB
+constexpr uint32_t W_Q = 0, W_K = QTILE, W_V = W_K + 2 * KTILE, W_BAR = W_V + 2 * KTILE;
+constexpr uint32_t W_XMAX = W_BAR + 256;   // float [2 key tiles][2 column halves][128 rows]
+constexpr uint32_t W_LSUM = W_XMAX + 2048;  // float [2 column halves][128 rows]
+constexpr uint32_t W_TOTAL = W_LSUM + 1024 + 1024;
+constexpr uint32_t COL_S = 0, COL_P = 128, COL_O = 256;
+constexpr long long W_WAIT_LIMIT = 1ll << 31;
+
+struct __align__(64) WParams {
+    CUtensorMap tq, tk, tv;
+    float* o;
+    int* err;
+    const float* vinv;
+    uint32_t qk_fmt, o_type;
+    uint32_t n_q, q_pad, n_k, k_pad, heads, kv_heads, q_pos0, block, width, n_tiles;
+    float scale_log2;
+};
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi)
+{
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(WNT, 1) attn_tc256_kernel(const __grid_constant__ WParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* const gbase = smem_raw + (base - raw);
+    const uint32_t sQ = base + W_Q, sK = base + W_K, sV = base + W_V, sB = base + W_BAR;
+    const uint32_t q_full = sB;
+    auto k_full = [&](uint32_t s) { return sB + 8 + 8 * s; };
+    auto k_empty = [&](uint32_t s) { return sB + 24 + 8 * s; };
+    auto v_full = [&](uint32_t s) { return sB + 40 + 8 * s; };
+    auto v_empty = [&](uint32_t s) { return sB + 56 + 8 * s; };
+    auto s_full = [&](uint32_t b) { return sB + 72 + 8 * b; };
+    auto s_free = [&](uint32_t b) { return sB + 88 + 8 * b; };
+    auto p_full = [&](uint32_t b) { return sB + 104 + 8 * b; };
+    const uint32_t pv_done = sB + 120, mma_done = sB + 128, tmem_slot = sB + 136;
+    volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t tile = p.n_tiles - 1 - blockIdx.x;  // the longest causal rows first
+    const uint32_t h = blockIdx.y, q0 = tile * WBM;
+    if (q0 >= p.n_q)
+        return;
+    const uint32_t kvh = h / (p.heads / p.kv_heads);
+    const uint32_t last = p.q_pos0 + min(q0 + WBM, p.n_q) - 1;
+    const uint32_t n_keys = last >= p.block ? p.n_k : min(p.n_k, last + 1);
+    const uint32_t nb = (n_keys + WBN - 1) / WBN;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (uint32_t s = 0; s < 2; ++s) {
+            mbar_init(k_full(s), 1);
+            mbar_init(k_empty(s), 1);
+            mbar_init(v_full(s), 1);
+            mbar_init(v_empty(s), 1);
+            mbar_init(s_full(s), 1);
+            mbar_init(s_free(s), 256);
+            mbar_init(p_full(s), 256);
+        }
+        mbar_init(pv_done, 1);
+        mbar_init(mma_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot_ptr;
+
+    if ((warp == 0 || warp == 2) && lane == 0) {
+        // ---------------- TMA producers: warp 0 Q and the K ring, warp 2 the V ring ----------------
+        const bool is_k = warp == 0;
+        const CUtensorMap* map = is_k ? &p.tk : &p.tv;
+        tma_prefetch_desc(map);
+        if (is_k) {
+            tma_prefetch_desc(&p.tq);
+            mbar_expect_tx(q_full, QTILE);
+            for (int dh = 0; dh < 4; ++dh)
+                tma_load_3d(sQ + dh * QBOX, &p.tq, q_full, dh * 64, int(q0), int(h));
+        }
+        bool ok = true;
+        uint32_t issued = 0;
+        for (uint32_t j = 0; j < nb; ++j) {
+            const uint32_t s = j & 1;
+            if (j >= 2 && !mbar_wait(is_k ? k_empty(s) : v_empty(s), ((j >> 1) & 1) ^ 1, W_WAIT_LIMIT)) {
+                ok = false;
+                break;
+            }
+            const uint32_t full = is_k ? k_full(s) : v_full(s), ring = is_k ? sK : sV;
+            mbar_expect_tx(full, KTILE);
+            for (int dh = 0; dh < 4; ++dh)
+                tma_load_3d(ring + s * KTILE + dh * KBOX, map, full, dh * 64, int(j * WBN), int(kvh));
+            ++issued;
+        }
+        if (!ok)
+            atomicExch(p.err, 31);
+        // our copies in flight land before the CTA leaves (already so on the normal path)
+        if (is_k)
+            mbar_wait(q_full, 0, W_WAIT_LIMIT);
+        for (uint32_t i = issued > 2 ? issued - 2 : 0; i < issued; ++i)
+            mbar_wait(is_k ? k_full(i & 1) : v_full(i & 1), (i >> 1) & 1, W_WAIT_LIMIT);
+    } else if (warp == 1) {
+        // ---------------- UMMA issuer ----------------
+        if (lane == 0 && nb > 0) {
+            const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, WBM, WBN);
+            const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, WBM, WD);
+            auto qk = [&](uint32_t j) {
+                const uint32_t s = j & 1;
+                bool w = mbar_wait(k_full(s), (j >> 1) & 1, W_WAIT_LIMIT);
+                if (w && j >= 2)  // S(j - 2) read by the softmax
+                    w = mbar_wait(s_free(s), ((j - 2) >> 1) & 1, W_WAIT_LIMIT);
+                if (!w)
+                    return false;
+                fence_after();
+#pragma unroll
+                for (uint32_t ks = 0; ks < WD / 16; ++ks)
+                    umma_ss(tmem + COL_S + s * 64, sdesc(sQ + (ks >> 2) * QBOX + (ks & 3) * 32, 16, 1024),
+                            sdesc(sK + s * KTILE + (ks >> 2) * KBOX + (ks & 3) * 32, 16, 1024), idesc_qk, ks > 0);
+                umma_commit(s_full(s));
+                umma_commit(k_empty(s));
+                return true;
+            };
+            bool ok = mbar_wait(q_full, 0, W_WAIT_LIMIT) && qk(0) && (nb < 2 || qk(1));
+            for (uint32_t j = 0; ok && j < nb; ++j) {
+                const uint32_t s = j & 1;
+                ok = mbar_wait(p_full(s), (j >> 1) & 1, W_WAIT_LIMIT) && mbar_wait(v_full(s), (j >> 1) & 1, W_WAIT_LIMIT);
+                if (!ok)
+                    break;
+                fence_after();
+#pragma unroll
+                for (uint32_t kk = 0; kk < WBN / 16; ++kk)
+                    umma_ts(tmem + COL_O, tmem + COL_P + s * 32 + kk * 8, sdesc(sV + s * KTILE + kk * 2048, KBOX, 1024),
+                            idesc_pv, j > 0 || kk > 0);
+                umma_commit(pv_done);
+                umma_commit(v_empty(s));
+                if (j + 2 < nb)
+                    ok = qk(j + 2);
+            }
+            if (!ok)
+                atomicExch(p.err, 32);
+            umma_commit(mma_done);  // every MMA issued above has finished before TMEM is freed
+            mbar_wait(mma_done, 0, W_WAIT_LIMIT);
+        }
+    } else if (warp >= 4) {
+        // ---------------- softmax and epilogue: row `row`, key columns 32c .. 32c + 31 of each tile ----------------
+        const uint32_t c = (warp - 4) >> 2, qd = warp & 3, row = qd * 32 + lane;
+        const uint32_t tl = tmem + ((qd * 32) << 16);
+        float* const xmax = reinterpret_cast<float*>(gbase + W_XMAX);
+        float* const lsum = reinterpret_cast<float*>(gbase + W_LSUM);
+        const uint32_t pos = p.q_pos0 + q0 + row;
+        const uint32_t lim = pos >= p.block ? p.n_k : min(p.n_k, pos + 1);  // this row sees keys [0, lim)
+        const uint32_t pos1 = p.q_pos0 + q0;
+        const uint32_t lim1 = pos1 >= p.block ? p.n_k : min(p.n_k, pos1 + 1);  // the tile's first row
+        const float scale = p.scale_log2;
+        const uint64_t scale2 = pack2(scale, scale);
+        float m = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (uint32_t j = 0; j < nb; ++j) {
+            const uint32_t b = j & 1;
+            uint32_t r[32];
+            float pmax = -INFINITY;
+            if (ok)
+                ok = __all_sync(0xffffffffu, mbar_wait(s_full(b), (j >> 1) & 1, W_WAIT_LIMIT));
+            if (ok) {
+                fence_after();
+                tmem_ld32(tl + COL_S + b * 64 + 32 * c, r);
+                tmem_wait_ld();
+                reg_fence(r);
+                fence_before();
+                mbar_arrive(s_free(b));  // QK(j + 2) may overwrite S(j) now
+                const uint32_t j0 = j * WBN + 32 * c;
+                if (j * WBN + WBN > lim1) {  // a tile the mask cuts: keys at or past this row's limit drop out
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (j0 + e >= lim)
+                            r[e] = 0xFF800000u;  // -inf
+                }
+                float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int e = 0; e < 32; e += 8)
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        mq[t] = max3f(mq[t], __uint_as_float(r[e + 2 * t]), __uint_as_float(r[e + 2 * t + 1]));
+                pmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+            }
+            // the row maximum over both column halves (partner: the same row in the other warpgroup)
+            xmax[(b * 2 + c) * 128 + row] = pmax;
+            named_bar(1 + qd, 64);
+            if (!ok)
+                continue;
+            const float mx = fmaxf(pmax, xmax[(b * 2 + (c ^ 1)) * 128 + row]) * scale;
+            float f = 1.0f;
+            bool resc = false;
+            if (mx > m + 8.0f) {
+                f = m == -INFINITY ? 0.0f : ex2(m - mx);
+                m = mx;
+                l *= f;
+                resc = true;
+            }
+            const float mneg = m == -INFINITY ? 0.0f : -m;
+            const uint64_t mneg2 = pack2(mneg, mneg);
+            uint32_t pk[16];
+            uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                float a, bb;
+                unpack2(ffma2(pack2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), scale2, mneg2), a, bb);
+                a = ex2(a);
+                bb = ex2(bb);
+                sum2[e & 1] = fadd2(sum2[e & 1], pack2(a, bb));
+                pk[e] = pack_h2(a, bb);
+            }
+            {
+                float s0, s1, s2, s3;
+                unpack2(sum2[0], s0, s1);
+                unpack2(sum2[1], s2, s3);
+                l += (s0 + s1) + (s2 + s3);
+            }
+            // A rescale of O waits for P.V(j - 1), which adds to it (P.V(j) waits for this thread's P(j); P.V(j - 2)
+            // finished before QK(j), committed after it).
+            if (j > 0 && __any_sync(0xffffffffu, resc)) {
+                ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, W_WAIT_LIMIT));
+                if (ok) {
+                    fence_after();
+                    const float g = resc ? f : 1.0f;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        uint32_t o[32];
+                        tmem_ld32(tl + COL_O + 128 * c + 32 * k, o);
+                        tmem_wait_ld();
+                        reg_fence(o);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * g);
+                        tmem_st32(tl + COL_O + 128 * c + 32 * k, o);
+                    }
+                }
+            }
+            tmem_st16(tl + COL_P + b * 32 + 16 * c, pk);
+            tmem_wait_st();
+            fence_before();
+            mbar_arrive(p_full(b));
+        }
+        // O is final once the issuer's last commit lands
+        if (ok && nb > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(mma_done, 0, W_WAIT_LIMIT));
+            fence_after();
+        }
+        if (!ok && lane == 0)
+            atomicExch(p.err, 33);
+        lsum[c * 128 + row] = l;
+        named_bar(1 + qd, 64);
+        l = lsum[row] + lsum[128 + row];
+        const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
+        const uint32_t grow = q0 + row;
+        const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(h) * WD + 128 * c;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t o[32];
+            if (ok && nb > 0) {
+                tmem_ld32(tl + COL_O + 128 * c + 32 * k, o);
+                tmem_wait_ld();
+                reg_fence(o);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e)
+                    o[e] = 0u;
+            }
+            if (grow < p.n_q)
+                out_store32(p.o, ooff + 32 * k, o, inv, p.o_type);
+        }
+    }
+    __syncwarp();
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_w()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// [heads][rows][256] 16-bit tiles, boxes of box_rows rows x 64 values, 128-byte swizzle, zero fill past `rows`.
+bool map256(CUtensorMap* map, const void* ptr, bool bf16, uint32_t rows, uint32_t heads, uint32_t box_rows)
+{
+    auto enc = encode_w();
+    if (!enc)
+        return false;
+    cuuint64_t dims[3] = {WD, rows, heads};
+    cuuint64_t strides[2] = {uint64_t(WD) * 2, uint64_t(rows) * WD * 2};
+    cuuint32_t box[3] = {64, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+} // namespace
+
+cudaError_t launch_attn_tc256(const AttnParams& a, int dtype, const void* v16, const float* vinv, int* err,
+                              cudaStream_t st)
+{
+    if (a.n_q == 0 || a.heads == 0)
+        return cudaSuccess;
+    WParams p;
+    const bool bf = dtype == kBF16;
+    if (!map256(&p.tq, a.q, bf, a.q_pad, a.heads, WBM) || !map256(&p.tk, a.k, bf, a.k_pad, a.kv_heads, WBN) ||
+        !map256(&p.tv, bf ? v16 : a.v, false, a.k_pad, a.kv_heads, WBN))
+        return cudaErrorInvalidValue;
+    p.o = a.o;
+    p.err = err;
+    p.vinv = bf ? vinv : nullptr;
+    p.qk_fmt = bf ? 1u : 0u;
+    p.o_type = a.o_type;
+    p.n_q = a.n_q;
+    p.q_pad = a.q_pad;
+    p.n_k = a.n_k;
+    p.k_pad = a.k_pad;
+    p.heads = a.heads;
+    p.kv_heads = a.kv_heads;
+    p.q_pos0 = a.q_pos0;
+    p.block = a.block;
+    p.width = a.width;
+    p.n_tiles = (a.q_pad + WBM - 1) / WBM;
+    p.scale_log2 = a.scale * kLog2e;
+    cudaError_t e = cudaFuncSetAttribute(attn_tc256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, W_TOTAL);
+    if (e != cudaSuccess)
+        return e;
+    attn_tc256_kernel<<<dim3(p.n_tiles, a.heads), WNT, W_TOTAL, st>>>(p);
+    return cudaGetLastError();
+}
+
+} // namespace mako

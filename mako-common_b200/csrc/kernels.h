@@ -43,6 +43,10 @@ cudaError_t launch_attn_mma(const AttnParams& p, int dtype, int dim, bool sparse
 // wait timed out.
 cudaError_t launch_attn_tc(const AttnParams& p, int dtype, int dim, const void* v16, const float* vinv, int* err,
                            cudaStream_t s);
+// Flash attention for 256-wide heads on sm_100a: one 128-row tile per CTA, 64-key K / V tiles.  bf16 inputs need
+// v16 / vinv from launch_v_to_f16 (dim 256).
+cudaError_t launch_attn_tc256(const AttnParams& p, int dtype, const void* v16, const float* vinv, int* err,
+                              cudaStream_t s);
 // Block-sparse attention for 128-wide heads on sm_100a: two query cubes per 128-row UMMA tile, their key-cube lists
 // walked in lockstep.  bf16 inputs need v16 / vinv (launch_v_to_f16 over all k_pad rows with the valid mask).
 cudaError_t launch_attn_tc_sparse(const AttnParams& p, int dtype, bool sel_i32, const void* v16, const float* vinv,

@@ -380,10 +380,9 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
     p.width = width;
     p.o_type = out_type(ctx, dtype);
     p.scale = 1.0f / sqrtf(float(dim));
-    const bool tc_ok = (dim == 64 || dim == 128) && ctx->cc_major == 10;
+    const bool tc_ok = ctx->cc_major == 10;
     if (ctx->prefill_kernel == 2 && !tc_ok)
-        return fail(MAKO_ENOTSUP, "attention: the tcgen05 kernel takes 64- or 128-wide heads on sm_100 (got %u, sm_%d)",
-                    dim, ctx->cc_major * 10);
+        return fail(MAKO_ENOTSUP, "attention: the tcgen05 kernels need sm_100 (sm_%d)", ctx->cc_major * 10);
     if (tc_ok && ctx->prefill_kernel != 1) {
         void *v16 = nullptr, *vmax = nullptr, *vinv = nullptr;
         if (dtype == MAKO_BF16) {
@@ -401,7 +400,9 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
         }
         ctx->launches += 1;
         KernelTimer t(ctx, st);
-        cudaError_t e = mako::launch_attn_tc(p, dtype, int(dim), v16, static_cast<const float*>(vinv), ctx->err, st);
+        cudaError_t e = dim == 256 ? mako::launch_attn_tc256(p, dtype, v16, static_cast<const float*>(vinv), ctx->err, st)
+                                   : mako::launch_attn_tc(p, dtype, int(dim), v16, static_cast<const float*>(vinv),
+                                                          ctx->err, st);
         t.stop();
         return launched("attention (tcgen05)", e);
     }

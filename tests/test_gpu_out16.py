@@ -48,7 +48,7 @@ def both(ctx, call, o32, o16, dtype):
 
 
 
-@pytest.mark.parametrize("dim", [64, 128])
+@pytest.mark.parametrize("dim", [64, 128, 256])
 @pytest.mark.parametrize("kernel", [0, 1], ids=["auto", "mma"])
 @pytest.mark.parametrize("dtype", [0, 1])
 def test_dense_out16(ctx, kernel, dtype, dim):

@@ -59,6 +59,9 @@ DENSE = [
                               dtype=0)),
     ("d256", dict(seed=7, heads=4, kv_heads=2, dim=256, n_q=190, n_k=190, dtype=0)),
     ("d256-bf16", dict(seed=8, heads=2, kv_heads=1, dim=256, n_q=64, n_k=300, block=0, dtype=1)),
+    ("d256-gqa-long", dict(seed=13, heads=8, kv_heads=1, dim=256, n_q=900, n_k=900, dtype=1)),
+    ("d256-offset-block", dict(seed=14, heads=3, kv_heads=3, dim=256, n_q=200, n_k=650, q_pos0=450, block=520,
+                               dtype=0)),
     ("video-rms", dict(seed=9, heads=2, kv_heads=2, dim=128, n_q=1000, n_k=1000, block=0, dtype=1, qk_rms_norm=True)),
     ("config3-scale", dict(seed=10, heads=4, kv_heads=1, dim=128, n_q=700, n_k=700, dtype=1, scale=0.5)),
 ]
@@ -67,9 +70,7 @@ DENSE = [
 @pytest.mark.parametrize("name,kw", DENSE, ids=[n for n, _ in DENSE])
 @pytest.mark.parametrize("kernel", [0, 1, 2], ids=["auto", "mma", "tcgen05"])
 def test_dense(ctx, oracle, name, kw, kernel):
-    """kernel 0: the default choice (tcgen05 for 64- and 128-wide heads), 1: the portable mma.sync kernel, 2: tcgen05."""
-    if kernel == 2 and kw["dim"] == 256:
-        pytest.skip("the tcgen05 kernel takes 64- and 128-wide heads")
+    """kernel 0: the default choice (tcgen05), 1: the portable mma.sync kernel, 2: tcgen05 explicitly."""
     case = C.dense_case(**kw)
     got = run_dense(ctx, case, kernel)
     assert ctx.device_error() == 0
@@ -344,19 +345,6 @@ def test_sparse_h3_layout(ctx, oracle, kernel, dtype):
     ok, stats = C.within(got[:L["n_out"]], want[:L["n_out"]])
     assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
     assert np.all(got[L["n_out"]:] == SENTINEL)
-
-
-def test_tcgen05_rejects_other_widths(ctx):
-    import torch
-    import mako_attn
-    q = torch.zeros(64 * 256, dtype=torch.float16, device="cuda")
-    o = torch.zeros(64 * 256, dtype=torch.float32, device="cuda")
-    ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 2)
-    try:
-        with pytest.raises(mako_attn.MakoError, match="tcgen05"):
-            ctx.attention(q, q, q, o, 10, 64, 10, 64, 1, 1, 0, 0, 256)
-    finally:
-        ctx.set_option(mako_attn.OPT_PREFILL_KERNEL, 0)
 
 
 def test_argument_errors(ctx):
