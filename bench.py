@@ -11,10 +11,12 @@ Workloads (synthetic seeded data -- no dataset is involve
   prefill_small  configs[0]: causal GQA prefill fp16, 16 / 8 heads, D 128, S 512
   decode_long    configs[1]'s variant: one sequence of 262144 fp16 keys, 32 / 8 heads, D 128
   heads          the head-tile producers (RMS norm + RoPE into bf16 tiles) at configs[2]'s shape
+  prefill_d256   not a BASELINE config: causal GQA prefill bf16 with Qwen3.5's 256-wide gated-attention heads,
+                 16 / 2 heads, S 8192
 A step is one call of the public C ABI (include/mako_attn.h) over one batch held in HBM; `value` is device time
 (CUDA events on the launching stream, L2 flushed between steps, max over ranks); `e2e` is the same metric with the
 step's inputs copied from pinned host memory and its output read back inside the timed region.  With N > 1 the
-decode / prefill_small / sparse workloads run one replica per GPU (weak scaling); prefill and bidir shard the heads
+decode / prefill_small / prefill_d256 / sparse workloads run one replica per GPU (weak scaling); prefill and bidir shard the heads
 over the GPUs with the output all-gather fused into the attention kernel, and decode_long shards the keys with a
 cross-GPU log-sum-exp combine (strong scaling: `value` is the one problem's work over the slowest rank's time).
 
@@ -535,8 +537,8 @@ def torch_int16():
 
 
 def make_workload(name, world=1, rank=0):
-    """The workload of `name` as rank `rank` of `world` sees it.  decode, sparse and prefill_small run one replica per
-    GPU; prefill and bidir shard heads, decode_long shards keys (one problem across the GPUs)."""
+    """The workload of `name` as rank `rank` of `world` sees it.  decode, sparse, prefill_small and prefill_d256 run
+    one replica per GPU; prefill and bidir shard heads, decode_long shards keys (one problem across the GPUs)."""
     if name == "decode":
         return Decode()
     if name == "decode_long":
@@ -547,6 +549,10 @@ def make_workload(name, world=1, rank=0):
     if name == "prefill_small":
         return Prefill("prefill_small", "prefill attention TFLOP/s (causal GQA)", 1, 16, 8, 128, 512, "fp16", 1.0,
                        UINT32_MAX, 0, cfg="prefill_small (configs[0])")
+    if name == "prefill_d256":
+        return Prefill("prefill_d256", "prefill attention TFLOP/s (causal GQA, 256-wide heads)", 1, 16, 2, 256, 8192,
+                       "bf16", 0.5, UINT32_MAX, 0,
+                       cfg="prefill_d256 (Qwen3.5 gated-attention head shape, synthetic; not a BASELINE config)")
     if name == "bidir":
         return Prefill("bidir", "bidirectional attention TFLOP/s (video DiT)", 1, 24, 24, 128, 75600, "bf16", 1.0, 0,
                        0, rms_qk=True, cfg="bidir (configs[4])", world=world, rank=rank)
@@ -853,7 +859,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "decode_long", "prefill", "sparse", "bidir", "prefill_small", "heads"])
+                    choices=["decode", "decode_long", "prefill", "sparse", "bidir", "prefill_small", "prefill_d256",
+                             "heads"])
     ap.add_argument("--impl", default="mako", choices=["mako", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
