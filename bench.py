@@ -14,11 +14,13 @@ Workloads (synthetic seeded data -- no dataset is involve
   prefill_d256   not a BASELINE config: causal GQA prefill bf16 with Qwen3.5's 256-wide gated-attention heads,
                  16 / 2 heads, S 8192
 A step is one call of the public C ABI (include/mako_attn.h) over one batch held in HBM; `value` is device time
-(CUDA events on the launching stream, L2 flushed between steps, max over ranks); `e2e` is the same metric with the
+(CUDA events on the launching stream, max over ranks; L2 flushed between steps by a 256 MB write, except for an
+HBM-bound step whose inputs exceed 4x the 126 MB L2, `config.l2` says which); `e2e` is the same metric with the
 step's inputs copied from pinned host memory and its output read back inside the timed region.  With N > 1 the
-decode / prefill_small / prefill_d256 / sparse workloads run one replica per GPU (weak scaling); prefill and bidir shard the heads
-over the GPUs with the output all-gather fused into the attention kernel, and decode_long shards the keys with a
-cross-GPU log-sum-exp combine (strong scaling: `value` is the one problem's work over the slowest rank's time).
+decode / prefill_small / prefill_d256 / sparse workloads run one replica per GPU (weak scaling); prefill and bidir
+shard the heads over the GPUs with the output all-gather fused into the attention kernel, and decode_long shards the
+keys with a cross-GPU log-sum-exp combine (strong scaling: `value` is the one problem's work over the slowest rank's
+time).
 
 --impl reference times the reference's scalar attention restated on the CPU (oracle/, all host threads) on a
 bounded sample of the same workload: the reference itself is Metal-only and cannot run here.
@@ -39,6 +41,7 @@ for p in (os.path.join(ROOT, "mako-common_b200"), os.path.join(ROOT, "oracle"), 
 
 UINT32_MAX = 0xFFFFFFFF
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+L2_BYTES = 126 << 20
 
 
 def peaks():
@@ -685,7 +688,20 @@ def run_mako(args):
             dist.all_gather_object(out, b, group=cpu_group)
             return out
         W.setup(ctx, world, rank, exchange)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE)
+    # Between timed steps L2 is flushed (a 256 MB write), except for HBM-bound steps whose inputs are more than 4x the
+    # L2: they cannot hit it across steps, and the flush's dirty lines would be written back inside the next step.
+    in_bytes = sum(t.numel() * t.element_size() for t in W.inputs)
+    flush = None
+    if W.bound == "hbm" and in_bytes >= 4 * L2_BYTES:
+        W.config["l2"] = (f"not flushed: the step's inputs ({in_bytes / 1e6:.0f} MB per GPU) are more than 4x the "
+                          "126 MB L2")
+    else:
+        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE)
+
+    def flush_l2():
+        if flush is not None:
+            flush.zero_()
+
     stream = torch.cuda.current_stream()
 
     clocks = Clocks(local)
@@ -698,7 +714,7 @@ def run_mako(args):
     barrier(world)
     clocks.mark_start()
     for _ in range(args.steps):
-        flush.zero_()
+        flush_l2()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         W.step(ctx)
@@ -722,7 +738,7 @@ def run_mako(args):
     e2e_times = []
     barrier(world)
     for i in range(args.warmup + args.steps):
-        flush.zero_()
+        flush_l2()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for d, h in zip(dev_in, host_in):
@@ -738,12 +754,12 @@ def run_mako(args):
     e2e_value = W.to_metric(W.total_work(world) / (e2e_ms / 1e3))
 
     # The dominant kernel alone: the library records a CUDA event pair around each call's main kernel on the
-    # launching stream (MAKO_OPT_KERNEL_TIMING), over another K steps with the same L2 flush.
+    # launching stream (MAKO_OPT_KERNEL_TIMING), over another K steps with the same L2 handling.
     ctx.set_option(mako_attn.OPT_KERNEL_TIMING, 1)
     ctx.kernel_times()
     barrier(world)
     for _ in range(args.steps):
-        flush.zero_()
+        flush_l2()
         W.step(ctx)
     kt = ctx.kernel_times()
     ctx.set_option(mako_attn.OPT_KERNEL_TIMING, 0)
