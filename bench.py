@@ -59,6 +59,18 @@ def round_up(x, m):
 
 # ---- workloads ------------------------------------------------------------------------------------------------------
 
+def l2_flushed(W):
+    """Whether L2 is flushed (a 256 MB write) between timed steps of W, recorded in W.config["l2"]: yes, except for
+    an HBM-bound step whose inputs are more than 4x the L2 -- it cannot hit L2 across steps, and the flush's dirty
+    lines would be written back inside the next step."""
+    in_bytes = sum(t.numel() * t.element_size() for t in W.inputs)
+    if W.bound == "hbm" and in_bytes >= 4 * L2_BYTES:
+        W.config["l2"] = (f"not flushed: the step's inputs ({in_bytes / 1e6:.0f} MB per GPU) are more than 4x the "
+                          "126 MB L2")
+        return False
+    return True
+
+
 class Workload:
     """Holds device inputs, knows its algorithmic work, runs one step through the C ABI."""
     name = ""
@@ -688,15 +700,7 @@ def run_mako(args):
             dist.all_gather_object(out, b, group=cpu_group)
             return out
         W.setup(ctx, world, rank, exchange)
-    # Between timed steps L2 is flushed (a 256 MB write), except for HBM-bound steps whose inputs are more than 4x the
-    # L2: they cannot hit it across steps, and the flush's dirty lines would be written back inside the next step.
-    in_bytes = sum(t.numel() * t.element_size() for t in W.inputs)
-    flush = None
-    if W.bound == "hbm" and in_bytes >= 4 * L2_BYTES:
-        W.config["l2"] = (f"not flushed: the step's inputs ({in_bytes / 1e6:.0f} MB per GPU) are more than 4x the "
-                          "126 MB L2")
-    else:
-        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE) if l2_flushed(W) else None
 
     def flush_l2():
         if flush is not None:
@@ -846,6 +850,7 @@ def run_reference(args):
     import oracle as O
     DEVICE = "cpu"
     W = make_workload(args.workload)
+    l2_flushed(W)  # the same config as the device arm
     threads = O.threads(0)
     run, work, sample = W.cpu_sample(O, threads)
     for _ in range(args.warmup):
