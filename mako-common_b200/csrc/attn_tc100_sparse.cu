@@ -10,15 +10,16 @@
 // partner's is padded with empty passes; an entry >= n_cubes is skipped.  Masking per key: valid[key] and the pass's
 // key range (ops.metal:1109); output row r goes to o row map[r], dropped when < 0 (ops.metal:1174-1184).
 //
-// One tile per CTA (384 threads): warp 0 issues the K loads and warp 2 the V loads (TMA, 64-row boxes so each half
-// can come from anywhere, into 3-stage rings), warp 1 issues UMMA, and warps 4-11 run the softmax and the epilogue:
-// each query row (TMEM lane) belongs to one thread of warps 4-7 and one of warps 8-11, which take half of the row's
-// columns each and agree on the row maximum through shared memory, so two warps per sub-partition share the exp unit.
-// TMEM (512 columns): S in two buffers (0-127, 128-255), O (256-383), Q (384-447, loaded once by the softmax threads,
-// the A operand of Q K^T so that product reads only K from shared memory) and P (448-511, fp16 pairs, the A operand
-// of P.V).  Q K^T of pass i + 2 waits only until the softmax has read S(i), so the tensor core runs Q K^T ahead while
-// the softmax works; the softmax writes P(i) once P.V(i - 1) has finished reading P(i - 1).  Precision, bounded waits
-// and the error flag as the dense kernel (attn_tc100.cu).
+// One tile per CTA (384 threads): warp 0 loads the tile's Q once and the K ring, warp 2 the V ring (TMA, 64-row boxes
+// for K and V so each half can come from anywhere; K in a 2-stage ring, V in a 3-stage ring), warp 1 issues UMMA, and
+// warps 4-11 run the softmax and the epilogue: each query row (TMEM lane) belongs to one thread of warps 4-7 and one
+// of warps 8-11, which take half of the row's columns each and agree on the row maximum through shared memory, so
+// two warps per sub-partition share the exp unit.
+// TMEM (512 columns): S in two buffers (0-127, 128-255), O (256-383) and P in two buffers (384-447, 448-511, fp16
+// pairs, the A operand of P.V); Q.K^T reads Q and K from shared memory.  The issue order is QK(0), QK(1), then per
+// pass PV(i), QK(i + 2): Q K^T(i + 2) waits only until the softmax has read S(i), and the softmax writes P(i) into
+// the buffer P.V(i - 2) read (finished before Q K^T(i), committed after it), so it waits for a product only to
+// rescale O.  Precision, bounded waits and the error flag as the dense kernel (attn_tc100.cu).
 #include "common.cuh"
 #include "kernels.h"
 #include "tc100.cuh"
@@ -32,21 +33,22 @@ namespace {
 
 using namespace tc;
 
-constexpr int SD = 128, SNT = 384, NST = 3;
+constexpr int SD = 128, SNT = 384, NSK = 2, NSV = 3;
 constexpr uint32_t DBOX = 128 * 64 * 2;  // one d-half of a 128-row tile: 16 KB
 constexpr uint32_t HBOX = 64 * 64 * 2;   // a 64-row x 64-value TMA box: 8 KB
 constexpr uint32_t STILE = 2 * DBOX;     // 128 rows x 128 values
-constexpr uint32_t S_K = 0, S_V = NST * STILE, S_BAR = 2 * NST * STILE;
+constexpr uint32_t S_Q = 0, S_K = STILE, S_V = S_K + NSK * STILE, S_BAR = S_V + NSV * STILE;
 constexpr uint32_t S_XMAX = S_BAR + 256;   // float [2 passes][2 column halves][128 rows]: partial row maxima
 constexpr uint32_t S_LSUM = S_XMAX + 2048;  // float [2 column halves][128 rows]: partial row sums
 constexpr uint32_t kListCache = 1024;        // list entries per cube kept in shared memory
 constexpr uint32_t S_LIST = S_LSUM + 1024;  // uint32 [2 cubes][kListCache]
 constexpr uint32_t S_TOTAL = S_LIST + 2 * kListCache * 4 + 1024;
-constexpr uint32_t COL_O = 256, COL_Q = 384, COL_P = 448;
+constexpr uint32_t COL_O = 256, COL_P = 384;  // P: two buffers of 64 columns
 constexpr long long S_WAIT_LIMIT = 1ll << 31;
 
 struct __align__(64) SpParams {
     CUtensorMap tk, tv;  // k and v (or the fp16 copy of v), 64-row boxes
+    CUtensorMap tq;      // q, 128-row boxes
     const void* q;
     float* o;
     int* err;
@@ -169,8 +171,9 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     auto v_empty = [&](uint32_t s) { return sB + 72 + 8 * s; };
     auto s_full = [&](uint32_t b) { return sB + 96 + 8 * b; };
     auto s_free = [&](uint32_t b) { return sB + 112 + 8 * b; };
-    const uint32_t p_full = sB + 128, pv_done = sB + 136, q_ready = sB + 144, mma_done = sB + 152;
-    const uint32_t tmem_slot = sB + 160;
+    auto p_full = [&](uint32_t b) { return sB + 128 + 8 * b; };
+    const uint32_t pv_done = sB + 144, q_full = sB + 152, mma_done = sB + 160;
+    const uint32_t tmem_slot = sB + 168;
     volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -179,7 +182,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     const TileInfo t = tile_info(p, u, h);
 
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < NST; ++s) {
+        for (uint32_t s = 0; s < 3; ++s) {
             mbar_init(k_full(s), 1);
             mbar_init(k_empty(s), 1);
             mbar_init(v_full(s), 1);
@@ -189,9 +192,10 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             mbar_init(s_full(b), 1);
             mbar_init(s_free(b), 256);
         }
-        mbar_init(p_full, 256);
+        mbar_init(p_full(0), 256);
+        mbar_init(p_full(1), 256);
         mbar_init(pv_done, 1);
-        mbar_init(q_ready, 256);
+        mbar_init(q_full, 1);
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
@@ -209,8 +213,14 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         if (t.np > 0) {
             const bool is_k = warp == 0;
             const CUtensorMap* map = is_k ? &p.tk : &p.tv;
-            const uint32_t ring = base + (is_k ? S_K : S_V);
+            const uint32_t ring = base + (is_k ? S_K : S_V), nst = is_k ? NSK : NSV;
             tma_prefetch_desc(map);
+            if (is_k) {  // the tile's Q, once
+                tma_prefetch_desc(&p.tq);
+                mbar_expect_tx(q_full, STILE);
+                for (int dh = 0; dh < 2; ++dh)
+                    tma_load_3d(base + S_Q + dh * DBOX, &p.tq, q_full, dh * 64, int(t.row0), int(h));
+            }
             bool ok = true;
             uint32_t issued = 0;
             uint32_t rawn[2] = {raw_entry(p, t, h, 0, 0), raw_entry(p, t, h, 0, 1)};
@@ -222,8 +232,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                     rawn[0] = raw_entry(p, t, h, i + 1, 0);
                     rawn[1] = raw_entry(p, t, h, i + 1, 1);
                 }
-                const uint32_t s = i % NST, ph = (i / NST) & 1;
-                if (i >= NST && !mbar_wait(is_k ? k_empty(s) : v_empty(s), ph ^ 1, S_WAIT_LIMIT)) {
+                const uint32_t s = i % nst, ph = (i / nst) & 1;
+                if (i >= nst && !mbar_wait(is_k ? k_empty(s) : v_empty(s), ph ^ 1, S_WAIT_LIMIT)) {
                     ok = false;
                     break;
                 }
@@ -237,8 +247,10 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             if (!ok)
                 atomicExch(p.err, 11);
             // Our copies in flight land before the CTA leaves (already so on the normal path).
-            for (uint32_t i = issued > NST ? issued - NST : 0; i < issued; ++i)
-                mbar_wait(is_k ? k_full(i % NST) : v_full(i % NST), (i / NST) & 1, S_WAIT_LIMIT);
+            if (is_k)
+                mbar_wait(q_full, 0, S_WAIT_LIMIT);
+            for (uint32_t i = issued > nst ? issued - nst : 0; i < issued; ++i)
+                mbar_wait(is_k ? k_full(i % nst) : v_full(i % nst), (i / nst) & 1, S_WAIT_LIMIT);
         }
     } else if (warp == 1) {
         // ---------------- UMMA issuer ----------------
@@ -250,8 +262,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, 128, 128);
             const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, 128, SD);
             auto qk = [&](uint32_t j) {
-                const uint32_t s = j % NST, b = j & 1;
-                bool w = mbar_wait(k_full(s), (j / NST) & 1, S_WAIT_LIMIT);
+                const uint32_t s = j % NSK, b = j & 1;
+                bool w = mbar_wait(k_full(s), (j / NSK) & 1, S_WAIT_LIMIT);
                 if (w && j >= 2)
                     w = mbar_wait(s_free(b), ((j - 2) >> 1) & 1, S_WAIT_LIMIT);
                 if (!w)
@@ -259,25 +271,26 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 fence_after();
 #pragma unroll
                 for (uint32_t ks = 0; ks < SD / 16; ++ks)
-                    umma_ts(tmem + b * 128, tmem + COL_Q + ks * 8,
+                    umma_ss(tmem + b * 128, sdesc(base + S_Q + (ks >> 2) * DBOX + (ks & 3) * 32, 16, 1024),
                             sdesc(base + S_K + s * STILE + (ks >> 2) * DBOX + (ks & 3) * 32, 16, 1024), idesc_qk,
                             ks > 0);
                 umma_commit(s_full(b));
                 return true;
             };
-            bool ok = mbar_wait(q_ready, 0, S_WAIT_LIMIT);
+            bool ok = mbar_wait(q_full, 0, S_WAIT_LIMIT);
             fence_after();
             ok = ok && qk(0) && (t.np < 2 || qk(1));
             for (uint32_t i = 0; ok && i < t.np; ++i) {
-                const uint32_t s = i % NST;
-                ok = mbar_wait(p_full, i & 1, S_WAIT_LIMIT) && mbar_wait(v_full(s), (i / NST) & 1, S_WAIT_LIMIT);
+                const uint32_t s = i % NSV;
+                ok = mbar_wait(p_full(i & 1), (i >> 1) & 1, S_WAIT_LIMIT) &&
+                     mbar_wait(v_full(s), (i / NSV) & 1, S_WAIT_LIMIT);
                 if (!ok)
                     break;
                 fence_after();
 #pragma unroll
                 for (uint32_t kk = 0; kk < 8; ++kk)
-                    umma_ts(tmem + COL_O, tmem + COL_P + kk * 8, sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024),
-                            idesc_pv, i > 0 || kk > 0);
+                    umma_ts(tmem + COL_O, tmem + COL_P + 64 * (i & 1) + kk * 8,
+                            sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024), idesc_pv, i > 0 || kk > 0);
                 umma_commit(pv_done);
                 if (i + 2 < t.np)
                     ok = qk(i + 2);
@@ -296,31 +309,6 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         const float scale = p.scale_log2;
         const uint64_t scale2 = pack2(scale, scale);
         bool ok = true;
-        {
-            // half c of this row of Q: 64 16-bit values = 32 TMEM columns (zeros past q_pad)
-            const uint32_t grow = t.row0 + row;
-            uint32_t qr[32];
-            if (t.active && grow < p.q_pad) {
-                const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) +
-                                                                  (uint64_t(h) * p.q_pad + grow) * SD + 64 * c);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const uint4 w = __ldg(src + k);
-                    qr[4 * k + 0] = w.x;
-                    qr[4 * k + 1] = w.y;
-                    qr[4 * k + 2] = w.z;
-                    qr[4 * k + 3] = w.w;
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < 32; ++k)
-                    qr[k] = 0u;
-            }
-            tmem_st32(tl + COL_Q + 32 * c, qr);
-            tmem_wait_st();
-            fence_before();
-            mbar_arrive(q_ready);
-        }
         // this row's cube list, copied to shared memory once (the loop reads it without global-load latency)
         uint32_t* const lcache = reinterpret_cast<uint32_t*>(gbase + S_LIST);
         const bool cached = t.cube && t.ncp <= kListCache;
@@ -339,10 +327,10 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         // cannot time out), so both column halves run the same number of passes.
         auto pass = [&](auto nch_tag, uint32_t i, uint32_t key0, uint32_t hi) {
             constexpr int NCH = decltype(nch_tag)::value;
-            const uint32_t b = i & 1;
-            // S columns of chunk k and the packed P columns it fills
+            const uint32_t b = i & 1, pb = COL_P + 64 * b;
+            // S columns of chunk k and the packed P columns (buffer b) it fills
             auto s_col = [&](int k) { return NCH == 1 ? b * 128 + 64 * hr + 32 * c : b * 128 + 64 * c + 32 * k; };
-            auto p_col = [&](int k) { return NCH == 1 ? COL_P + 32 * hr + 16 * c : COL_P + 32 * c + 16 * k; };
+            auto p_col = [&](int k) { return NCH == 1 ? pb + 32 * hr + 16 * c : pb + 32 * c + 16 * k; };
             uint32_t r[32];
             float pmax = -INFINITY;
             if (ok) {
@@ -401,15 +389,14 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 l += (s0 + s1) + (s2 + s3);
             };
             exps();  // the chunk still in registers (the last one read)
-            // P.V(i - 1) must have finished: it reads the P columns written below and adds to the O rescaled below.
-            if (i > 0) {
+            // A rescale of O waits for P.V(i - 1), which adds to it (P.V(i) waits for this thread's P(i)); P(i)'s
+            // buffer was last read by P.V(i - 2), which finished before Q K^T(i) (committed after it).
+            if (i > 0 && __any_sync(0xffffffffu, resc)) {
                 ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, S_WAIT_LIMIT));
                 if (!ok)
                     return;
                 fence_after();
-                if (threadIdx.x == 128)
-                    mbar_arrive(v_empty((i - 1) % NST));  // PV(i - 1) has finished reading V(i - 1)
-                if (__any_sync(0xffffffffu, resc)) {
+                {
                     const float g = resc ? f : 1.0f;
 #pragma unroll
                     for (int k = 0; k < 2; ++k) {
@@ -427,7 +414,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             tmem_st16(tl + p_col(NCH - 1), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
             if (NCH == 1) {
                 // the other cube's packed columns of this row are zeros
-                tmem_st16_zero(tl + COL_P + 32 * (hr ^ 1) + 16 * c);
+                tmem_st16_zero(tl + pb + 32 * (hr ^ 1) + 16 * c);
             } else {
                 tmem_ld32(tl + s_col(0), r);
                 tmem_wait_ld();
@@ -440,7 +427,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             }
             tmem_wait_st();
             fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(p_full(b));
         };
 
         for (uint32_t i = 0; i < t.np; ++i) {
@@ -451,15 +438,18 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                     hi);
             if (ok)
                 ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, S_WAIT_LIMIT));
-            if (ok && threadIdx.x == 128)
-                mbar_arrive(k_empty(i % NST));  // QK(i) has finished reading K(i)
+            if (ok && threadIdx.x == 128) {
+                mbar_arrive(k_empty(i % NSK));  // QK(i) has finished reading K(i)
+                if (i >= 2)
+                    mbar_arrive(v_empty((i - 2) % NSV));  // and PV(i - 2), committed before it, V(i - 2)
+            }
             if (half)
                 pass(std::integral_constant<int, 1>{}, i, j0 + 32 * c, hi);
             else
                 pass(std::integral_constant<int, 2>{}, i, j0 + 64 * c, hi);
         }
-        if (ok && t.np > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (t.np - 1) & 1, S_WAIT_LIMIT));
+        if (ok && t.np > 0) {  // O is final once the issuer's last commit lands
+            ok = __all_sync(0xffffffffu, mbar_wait(mma_done, 0, S_WAIT_LIMIT));
             fence_after();
         }
         if (!ok && lane == 0)
@@ -540,8 +530,9 @@ cudaError_t launch_attn_tc_sparse(const AttnParams& a, int dtype, bool sel_i32, 
         return cudaSuccess;
     SpParams p;
     const bool bf = dtype == kBF16;
-    if (!map_rows(&p.tk, a.k, bf, a.k_pad, a.kv_heads, 64) || !map_rows(&p.tv, bf ? v16 : a.v, false, a.k_pad,
-                                                                         a.kv_heads, 64))
+    if (!map_rows(&p.tk, a.k, bf, a.k_pad, a.kv_heads, 64) ||
+        !map_rows(&p.tv, bf ? v16 : a.v, false, a.k_pad, a.kv_heads, 64) ||
+        !map_rows(&p.tq, a.q, bf, a.q_pad, a.heads, 128))
         return cudaErrorInvalidValue;
     p.q = a.q;
     p.o = a.o;
