@@ -38,8 +38,8 @@ enum {
 
 /* Options for mako_attn_set_option. */
 enum {
-    /* Dense attention kernel for 128-wide heads: 0 automatic (tcgen05 where built), 1 the portable mma.sync kernel,
-     * 2 the tcgen05 kernel (MAKO_ENOTSUP where it cannot run). */
+    /* Dense and block-sparse attention kernels: 0 automatic (the tcgen05 kernels on sm_100, every head width), 1 the
+     * portable mma.sync kernels, 2 the tcgen05 kernels (MAKO_ENOTSUP where they cannot run). */
     MAKO_OPT_PREFILL_KERNEL = 1,
     /* 1 (default): mako_attention with n_q == 1 runs the split-KV decode kernel; 0: the prefill kernel. */
     MAKO_OPT_DECODE_ROUTE = 2,
