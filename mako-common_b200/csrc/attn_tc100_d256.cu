@@ -8,7 +8,8 @@
 //
 // Warp roles (384 threads): warp 0 loads Q once and the K ring, warp 2 the V ring (TMA, 128-byte swizzle, boxes of
 // 64 values), warp 1's elected thread issues UMMA in the fixed order QK(0), QK(1), then per key tile PV(j),
-// QK(j + 2), with a commit after each group for the consumer and one releasing the ring stage it read.  Warps 4-11
+// QK(j + 2), with a commit after each group for its consumer and, after P.V, one releasing the V stage (a softmax
+// thread releases the K stage when it sees S(j), which Q.K^T(j) finished reading).  Warps 4-11
 // run the softmax: query row r (TMEM lane r) belongs to one thread of warps 4-7 (scores 0-31 of a key tile) and one
 // of warps 8-11 (scores 32-63), which agree on the row maximum through shared memory.
 // TMEM: S in two buffers (0-63, 64-127), P in two buffers (128-159, 160-191, fp16 pairs, the A operand of P.V) and O
@@ -157,7 +158,6 @@ __global__ void __launch_bounds__(WNT, 1) attn_tc256_kernel(const __grid_constan
                     umma_ss(tmem + COL_S + s * 64, sdesc(sQ + (ks >> 2) * QBOX + (ks & 3) * 32, 16, 1024),
                             sdesc(sK + s * KTILE + (ks >> 2) * KBOX + (ks & 3) * 32, 16, 1024), idesc_qk, ks > 0);
                 umma_commit(s_full(s));
-                umma_commit(k_empty(s));
                 return true;
             };
             bool ok = mbar_wait(q_full, 0, W_WAIT_LIMIT) && qk(0) && (nb < 2 || qk(1));
@@ -208,6 +208,8 @@ __global__ void __launch_bounds__(WNT, 1) attn_tc256_kernel(const __grid_constan
                 reg_fence(r);
                 fence_before();
                 mbar_arrive(s_free(b));  // QK(j + 2) may overwrite S(j) now
+                if (threadIdx.x == 128)
+                    mbar_arrive(k_empty(b));  // QK(j) has finished reading K(j)
                 const uint32_t j0 = j * WBN + 32 * c;
                 if (j * WBN + WBN > lim1) {  // a tile the mask cuts: keys at or past this row's limit drop out
 #pragma unroll
