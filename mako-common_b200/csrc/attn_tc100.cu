@@ -480,39 +480,10 @@ __global__ void __launch_bounds__(256) vconv_kernel(const __nv_bfloat16* v, __ha
 
 // ---- host ----------------------------------------------------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }();
-    return fn;
-}
-
-// [heads][rows][dim] 16-bit tiles, boxes of 128 rows x 64 values, 128-byte swizzle, zero fill past `rows`.
-bool head_map(CUtensorMap* map, const void* ptr, bool bf16, uint32_t dim, uint32_t rows, uint32_t heads)
-{
-    auto enc = encode_fn();
-    if (!enc)
-        return false;
-    cuuint64_t dims[3] = {dim, rows, heads};
-    cuuint64_t strides[2] = {uint64_t(dim) * 2, uint64_t(rows) * dim * 2};
-    cuuint32_t box[3] = {64, 128, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // o [n_q][width] fp32 as a TMA store target: boxes of 128 rows x 32 floats (128 bytes, 128-byte swizzle).
 bool out_map(CUtensorMap* map, float* o, uint32_t n_q, uint32_t width)
 {
-    auto enc = encode_fn();
+    auto enc = tensor_map_encoder();
     if (!enc)
         return false;
     cuuint64_t dims[2] = {width, n_q};
@@ -554,8 +525,9 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, int dim, const void* 
         return cudaErrorInvalidValue;
     TcParams p;
     const bool bf = dtype == kBF16;
-    if (!head_map(&p.tq, a.q, bf, dim, a.q_pad, a.heads) || !head_map(&p.tk, a.k, bf, dim, a.k_pad, a.kv_heads) ||
-        !head_map(&p.tv, bf ? v16 : a.v, false, dim, a.k_pad, a.kv_heads))
+    if (!tile_map(&p.tq, a.q, bf, dim, a.q_pad, a.heads, TBM) ||
+        !tile_map(&p.tk, a.k, bf, dim, a.k_pad, a.kv_heads, TBN) ||
+        !tile_map(&p.tv, bf ? v16 : a.v, false, dim, a.k_pad, a.kv_heads, TBN))
         return cudaErrorInvalidValue;
     if (a.n_od == 0) {
         p.od[0] = a.o;

@@ -321,35 +321,6 @@ __global__ void __launch_bounds__(WNT, 1) attn_tc256_kernel(const __grid_constan
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_w()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }();
-    return fn;
-}
-
-// [heads][rows][256] 16-bit tiles, boxes of box_rows rows x 64 values, 128-byte swizzle, zero fill past `rows`.
-bool map256(CUtensorMap* map, const void* ptr, bool bf16, uint32_t rows, uint32_t heads, uint32_t box_rows)
-{
-    auto enc = encode_w();
-    if (!enc)
-        return false;
-    cuuint64_t dims[3] = {WD, rows, heads};
-    cuuint64_t strides[2] = {uint64_t(WD) * 2, uint64_t(rows) * WD * 2};
-    cuuint32_t box[3] = {64, box_rows, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 } // namespace
 
 cudaError_t launch_attn_tc256(const AttnParams& a, int dtype, const void* v16, const float* vinv, int* err,
@@ -359,8 +330,9 @@ cudaError_t launch_attn_tc256(const AttnParams& a, int dtype, const void* v16, c
         return cudaSuccess;
     WParams p;
     const bool bf = dtype == kBF16;
-    if (!map256(&p.tq, a.q, bf, a.q_pad, a.heads, WBM) || !map256(&p.tk, a.k, bf, a.k_pad, a.kv_heads, WBN) ||
-        !map256(&p.tv, bf ? v16 : a.v, false, a.k_pad, a.kv_heads, WBN))
+    if (!tile_map(&p.tq, a.q, bf, WD, a.q_pad, a.heads, WBM) ||
+        !tile_map(&p.tk, a.k, bf, WD, a.k_pad, a.kv_heads, WBN) ||
+        !tile_map(&p.tv, bf ? v16 : a.v, false, WD, a.k_pad, a.kv_heads, WBN))
         return cudaErrorInvalidValue;
     p.o = a.o;
     p.err = err;

@@ -493,34 +493,6 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_sp()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }();
-    return fn;
-}
-
-bool map_rows(CUtensorMap* map, const void* ptr, bool bf16, uint32_t rows, uint32_t heads, uint32_t box_rows)
-{
-    auto enc = encode_sp();
-    if (!enc)
-        return false;
-    cuuint64_t dims[3] = {SD, rows, heads};
-    cuuint64_t strides[2] = {uint64_t(SD) * 2, uint64_t(rows) * SD * 2};
-    cuuint32_t box[3] = {64, box_rows, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 } // namespace
 
 cudaError_t launch_attn_tc_sparse(const AttnParams& a, int dtype, bool sel_i32, const void* v16, const float* vinv,
@@ -530,9 +502,9 @@ cudaError_t launch_attn_tc_sparse(const AttnParams& a, int dtype, bool sel_i32, 
         return cudaSuccess;
     SpParams p;
     const bool bf = dtype == kBF16;
-    if (!map_rows(&p.tk, a.k, bf, a.k_pad, a.kv_heads, 64) ||
-        !map_rows(&p.tv, bf ? v16 : a.v, false, a.k_pad, a.kv_heads, 64) ||
-        !map_rows(&p.tq, a.q, bf, a.q_pad, a.heads, 128))
+    if (!tile_map(&p.tk, a.k, bf, SD, a.k_pad, a.kv_heads, 64) ||
+        !tile_map(&p.tv, bf ? v16 : a.v, false, SD, a.k_pad, a.kv_heads, 64) ||
+        !tile_map(&p.tq, a.q, bf, SD, a.q_pad, a.heads, 128))
         return cudaErrorInvalidValue;
     p.q = a.q;
     p.o = a.o;

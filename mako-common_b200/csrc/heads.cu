@@ -5,8 +5,9 @@
 //
 // HBM-bound: a warp takes one output row of up to 8 heads, each lane dim / 32 consecutive values of each (128-bit
 // loads for 128-wide heads, the 8 heads' loads in flight together, the row's angles and the norm weights read once);
-// a head's sum of squares is a warp reduction (the row's heads reduce interleaved); rotation partners (i with i + rot / 2, or 2i with 2i + 1) come from
-// the same lane, a shuffle, or a per-warp shared-memory copy of the row when the pairing crosses lanes unevenly.
+// a head's sum of squares is a warp reduction (the row's heads reduce interleaved); rotation partners (i with
+// i + rot / 2, or 2i with 2i + 1) come from the same lane, a shuffle, or a per-warp shared-memory copy of the row when
+// the pairing crosses lanes unevenly.
 #include "kernels.h"
 
 #include <cuda_bf16.h>

@@ -3,6 +3,8 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace mako {
@@ -270,6 +272,40 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t a_fmt, uint32_t b_fmt,
 {
     return (1u << 4)            // D format fp32
            | (a_fmt << 7) | (b_fmt << 10) | (a_mn << 15) | (b_mn << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// ---- tensor maps (host) -------------------------------------------------------------------------------------------
+
+// cuTensorMapEncodeTiled, looked up once through the runtime (null where the driver does not provide it).
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// [heads][rows][dim] 16-bit tiles as a TMA source: boxes of box_rows rows x 64 values (128 bytes, the 128-byte
+// swizzle the UMMA descriptors above expect), zero fill past `rows`.
+inline bool tile_map(CUtensorMap* map, const void* ptr, bool bf16, uint32_t dim, uint32_t rows, uint32_t heads,
+                     uint32_t box_rows)
+{
+    auto enc = tensor_map_encoder();
+    if (!enc)
+        return false;
+    cuuint64_t dims[3] = {dim, rows, heads};
+    cuuint64_t strides[2] = {uint64_t(dim) * 2, uint64_t(rows) * dim * 2};
+    cuuint32_t box[3] = {64, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 } // namespace tc
