@@ -1,0 +1,47 @@
+"""bench.py's reference arm (the restated CPU attention on the host's cores) as the driver runs it: one JSON line with
+the contract's keys, and under torchrun with two ranks exactly one line (rank 0) while both ranks exit 0.  Runs on
+CPU; the device arm needs a B200 and is exercised by the GPU runs."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+KEYS = {"impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+        "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"}
+
+
+def json_lines(out):
+    return [json.loads(line) for line in out.splitlines() if line.startswith("{")]
+
+
+def check_line(d):
+    assert KEYS <= set(d), KEYS - set(d)
+    assert d["impl"] == "reference" and d["value"] > 0 and d["higher_is_better"] is True
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
+    assert "l2" in d["config"] and d["config"]["workload"]
+
+
+def test_reference_arm_one_rank():
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "3"], cwd=ROOT,
+                       capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = json_lines(r.stdout)
+    assert len(lines) == 1
+    check_line(lines[0])
+    assert lines[0]["metric"].startswith("decode") and lines[0]["n_gpus"] == 1
+
+
+def test_reference_arm_two_ranks():
+    env = dict(os.environ, OMP_NUM_THREADS="2")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", "29571", "bench.py", "--impl", "reference",
+                        "--gpus", "2", "--workload", "prefill_small", "--steps", "1", "--warmup", "3"], cwd=ROOT,
+                       capture_output=True, text=True, timeout=900, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = json_lines(r.stdout)
+    assert len(lines) == 1, r.stdout[-2000:]
+    check_line(lines[0])
+    assert lines[0]["n_gpus"] == 2
