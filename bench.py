@@ -4,10 +4,11 @@
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl mako|reference]
 
 Workloads (synthetic seeded data -- no dataset is involved):
-  decode         configs[1]: GQA decode fp16, batch 8, 32 q / 8 kv heads, D 128, KV lengths U[16384, 32768]  (default)
+  decode         configs[1]: GQA decode fp16, batch 8, 32 q / 8 kv heads, D 128, KV lengths U[16384, 32768]
   prefill        configs[2]: causal GQA prefill bf16, batch 2 (folded into heads), 32 / 8 heads, D 128, S 8192
   sparse         configs[3]: block-sparse bf16, 24 heads, D 128, S 16384, 64x64 blocks, diagonal + 15% per row
-  bidir          configs[4]: bidirectional bf16, 24 heads, D 128, N 75600, RMS-normalised q and k
+  bidir          configs[4]: bidirectional bf16, 24 heads, D 128, N 75600, RMS-normalised q and k  (default: the
+                 north star's head-sharded scaling config)
   prefill_small  configs[0]: causal GQA prefill fp16, 16 / 8 heads, D 128, S 512
   decode_long    configs[1]'s variant: one sequence of 262144 fp16 keys, 32 / 8 heads, D 128
   heads          the head-tile producers (RMS norm + RoPE into bf16 tiles) at configs[2]'s shape
@@ -164,9 +165,9 @@ class Decode(Workload):
                              self.D, self.S)
 
     # CPU sample: the whole workload (the oracle decode is a few seconds on a host)
-    def cpu_sample(self, O, threads, frac=1.0):
+    def cpu_sample(self, O, threads, target_s=None):
         import numpy as np
-        nb = max(1, int(round(self.B * frac)))
+        nb = self.B  # the whole batch: a few tenths of a second on a host
         q = self.q[:nb].cpu().view(torch_int16()).numpy().view(np.uint16)
         k = self.k[:nb].cpu().view(torch_int16()).numpy().view(np.uint16)
         v = self.v[:nb].cpu().view(torch_int16()).numpy().view(np.uint16)
@@ -299,17 +300,17 @@ class Prefill(Workload):
         # rows per second on this host, from a small probe, then a sample sized for ~target_s
         probe = self.sample_rows(8)
         t0 = time.perf_counter()
-        O.attention(code, q, k, v, self.S, self.q_pad, self.S, self.k_pad, self.heads, self.kv_heads, 0, self.block,
-                    self.D, rows=probe, nthreads=threads)
+        O.attention(code, q, k, v, self.S, self.q_pad, self.S, self.k_pad, self.heads_all, self.kv_all, 0,
+                    self.block, self.D, rows=probe, nthreads=threads)
         dt = max(time.perf_counter() - t0, 1e-3)
         n = int(min(self.S, max(8, len(probe) * target_s / dt)))
         rows = self.sample_rows(n)
-        work = float(sum(4 * self.D * self.heads * self.visible(int(i)) for i in rows))
+        work = float(sum(4 * self.D * self.heads_all * self.visible(int(i)) for i in rows))
 
         def run():
-            return O.attention(code, q, k, v, self.S, self.q_pad, self.S, self.k_pad, self.heads, self.kv_heads, 0,
+            return O.attention(code, q, k, v, self.S, self.q_pad, self.S, self.k_pad, self.heads_all, self.kv_all, 0,
                                self.block, self.D, rows=rows, nthreads=threads)
-        return run, work, f"{len(rows)} of {self.S} query rows (evenly spaced), all {self.heads} heads; " \
+        return run, work, f"{len(rows)} of {self.S} query rows (evenly spaced), all {self.heads_all} heads; " \
                           "rate extrapolated linearly in rows"
 
     def check(self, O):
@@ -391,7 +392,7 @@ class DecodeLong(Workload):
             DEVICE = dev
         return q, k, v
 
-    def cpu_sample(self, O, threads, frac=1.0):
+    def cpu_sample(self, O, threads, target_s=None):
         import numpy as np
         q, k, v = self._full()
         lens = np.array([self.L], np.int32)
@@ -516,7 +517,7 @@ class Heads(Workload):
             ctx.heads_partial(self.xv[rows], KV * D, 0, D, D, 0, KV, T, T, None, None, 0.0,
                               self.vh[b * KV:(b + 1) * KV])
 
-    def cpu_sample(self, O, threads, frac=1.0):
+    def cpu_sample(self, O, threads, target_s=None):
         xq = self.xq[:self.T].cpu().numpy()
         cs = self.cs.cpu().numpy()
         wq = self.wq.cpu().numpy()
@@ -669,6 +670,12 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def arm_config(W, world):
+    """The config both arms print at N GPUs: the workload's own keys and how the N GPUs share it."""
+    return dict(W.config, parallelism=("single GPU" if world == 1 else
+                                       (f"sharded x{world}" if W.scaling == "strong" else f"replica x{world}")))
+
+
 def read_traffic(name):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary (None if not captured)."""
     path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
@@ -808,9 +815,7 @@ def run_mako(args):
             "metric": W.metric, "value": round(value, 3), "unit": W.unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": W.scaling,
             "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded normal)",
-            "config": dict(W.config, parallelism=("single GPU" if world == 1 else
-                                                  (f"sharded x{world}" if W.scaling == "strong"
-                                                   else f"replica x{world}"))),
+            "config": arm_config(W, world),
             "e2e": {"value": round(e2e_value, 3), "unit": W.unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": launches, "roofline": roof, "clocks": clk, "parity": parity, "cpu_baseline": cpu,
@@ -849,10 +854,13 @@ def run_reference(args):
         return
     import oracle as O
     DEVICE = "cpu"
-    W = make_workload(args.workload)
-    l2_flushed(W)  # the same config as the device arm
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    W = make_workload(args.workload, world, 0)  # rank 0's view at N GPUs: the same config as the device arm
+    l2_flushed(W)
     threads = O.threads(0)
-    run, work, sample = W.cpu_sample(O, threads)
+    # each step a bounded sample: the whole --warmup + --steps run takes about two and a half minutes of CPU time
+    target_s = min(10.0, max(0.5, 150.0 / max(1, args.steps + args.warmup)))
+    run, work, sample = W.cpu_sample(O, threads, target_s=target_s)
     for _ in range(args.warmup):
         run()
     ts = []
@@ -864,8 +872,8 @@ def run_reference(args):
     value = W.to_metric(work / dt)
     line = {"impl": "reference", "metric": W.metric, "value": round(value, 6), "unit": W.unit,
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": W.dtype, "data": "synthetic (seeded normal)", "config": W.config,
+            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None,
+            "dtype": W.dtype, "data": "synthetic (seeded normal)", "config": arm_config(W, world),
             "cpu_baseline": {"value": round(value, 6), "unit": W.unit, "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 6), "unit": W.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -879,7 +887,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="decode",
+    ap.add_argument("--workload", default="bidir",
                     choices=["decode", "decode_long", "prefill", "sparse", "bidir", "prefill_small", "prefill_d256",
                              "heads"])
     ap.add_argument("--impl", default="mako", choices=["mako", "reference"])

@@ -25,13 +25,14 @@ def check_line(d):
 
 
 def test_reference_arm_one_rank():
-    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "3"], cwd=ROOT,
-                       capture_output=True, text=True, timeout=900)
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "decode", "--steps", "1",
+                        "--warmup", "3"], cwd=ROOT, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = json_lines(r.stdout)
     assert len(lines) == 1
     check_line(lines[0])
     assert lines[0]["metric"].startswith("decode") and lines[0]["n_gpus"] == 1
+    assert lines[0]["config"]["parallelism"] == "single GPU"
 
 
 def test_reference_arm_two_ranks():
@@ -45,3 +46,5 @@ def test_reference_arm_two_ranks():
     assert len(lines) == 1, r.stdout[-2000:]
     check_line(lines[0])
     assert lines[0]["n_gpus"] == 2
+    # the device arm's rank 0 prints the same config at N = 2 (bench.arm_config), so the two lines compare
+    assert lines[0]["config"]["parallelism"] == "replica x2"
