@@ -38,8 +38,9 @@ enum {
 
 /* Options for mako_attn_set_option. */
 enum {
-    /* Dense and block-sparse attention kernels: 0 automatic (the tcgen05 kernels on sm_100, every head width), 1 the
-     * portable mma.sync kernels, 2 the tcgen05 kernels (MAKO_ENOTSUP where they cannot run). */
+    /* Dense and block-sparse attention kernels: 0 (default) and 2 the tcgen05 kernels, every head width
+     * (MAKO_ENOTSUP on a device other than sm_100); 1 the mma.sync kernels, kept as the baseline that tests and
+     * benchmarks compare against, never chosen automatically. */
     MAKO_OPT_PREFILL_KERNEL = 1,
     /* 1 (default): mako_attention with n_q == 1 runs the split-KV decode kernel; 0: the prefill kernel. */
     MAKO_OPT_DECODE_ROUTE = 2,
@@ -94,7 +95,8 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
 
 /* Batched single-token decode over a KV cache of varying lengths: q [batch][heads][dim],
  * k and v [batch][kv_heads][k_stride][dim], kv_len [batch] int32 on the device (each at most max_kv_len and at most
- * k_stride), o [batch][heads * dim] floats.  Sequence b's query attends keys [0, kv_len[b]); a length <= 0 gives 0.
+ * k_stride), o [batch][heads * dim] floats.  Sequence b's query attends keys [0, kv_len[b]); a length <= 0 gives 0,
+ * and a length above max_kv_len is read as max_kv_len (no key past it is read, every o row is still written).
  * No reference counterpart kernel: the reference's decode step is mako_attention's form with n_q = 1,
  * q_pos0 = len - 1, block = UINT32_MAX (src/models/runtime.cpp:262-273), looped over sequences by the caller. */
 int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, const void* k, const void* v,
@@ -109,8 +111,10 @@ int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const voi
  * file-scope device array of 4 MiB that every GPU loading this library holds until the process exits; the call
  * picks larger splits when needed so that they fit, and returns MAKO_EINVAL when even one split per sequence would
  * not (batch * heads * (4 * dim + 8) bytes above 4 MiB).  The first call on each device looks up the array's device
- * address (cudaGetSymbolAddress); make that first call before any stream capture.  Every call uses the same array,
- * so calls that overlap on the GPU (other streams, other threads) race: serialise them. */
+ * address (cudaGetSymbolAddress) and remembers it; make that first call before any stream capture, and do not call
+ * it on a device again after cudaDeviceReset there (the remembered address belonged to the destroyed context).
+ * Every call uses the same array, so calls that overlap on the GPU (other streams, other threads) race: serialise
+ * them. */
 int mako_attention_decode_noalloc(void* stream, int dtype, const void* q, const void* k, const void* v, float* o,
                                   uint32_t batch, const int32_t* kv_len, uint32_t max_kv_len, uint32_t heads,
                                   uint32_t kv_heads, uint32_t dim, uint32_t k_stride);

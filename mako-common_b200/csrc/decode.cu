@@ -24,6 +24,16 @@ namespace {
 constexpr int DBN = 64, DNT = 128, DST = 3, QR = 16;
 constexpr uint64_t kMaxSplits = 1024;
 
+// Keys of sequence b: its kv_len entry (<= 0: none) capped at max_kv_len, so that a length beyond the split plan's
+// reach is cut at max_kv_len and every kernel of a call agrees on the same split count; without kv_len, p.len.
+__device__ __forceinline__ uint32_t seq_keys(const DecodeParams& p, uint32_t b)
+{
+    if (!p.kv_len)
+        return p.len;
+    const int32_t l = p.kv_len[b];
+    return l > 0 ? min(uint32_t(l), p.len) : 0u;
+}
+
 template <int D, typename T>
 __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams p)
 {
@@ -35,8 +45,7 @@ __global__ void __launch_bounds__(DNT, 2) decode_split_kernel(const DecodeParams
     const uint32_t group = p.heads / p.kv_heads, rb = (group + QR - 1) / QR;
     const uint32_t b = blockIdx.z, kvh = blockIdx.y / rb, rblk = blockIdx.y % rb, split = blockIdx.x;
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");  // the combine may be scheduled now
-    const int32_t lraw = p.kv_len ? p.kv_len[b] : int32_t(p.len);
-    const uint32_t L = lraw > 0 ? uint32_t(lraw) : 0u;
+    const uint32_t L = seq_keys(p, b);
     const uint32_t start = split * p.chunk;
     const uint32_t h0 = kvh * group + rblk * QR, nrows = min(uint32_t(QR), group - rblk * QR);
     if (start >= L) {
@@ -223,8 +232,7 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeParams p)
     __shared__ float w[kMaxSplits];
     __shared__ float tot;
     const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-    const int32_t lraw = p.kv_len ? p.kv_len[b] : int32_t(p.len);
-    const uint32_t L = lraw > 0 ? uint32_t(lraw) : 0u;
+    const uint32_t L = seq_keys(p, b);
     const uint32_t ns = min((L + p.chunk - 1) / p.chunk, p.n_splits);
     if (ns <= 1)  // written by kernel 1 (one split, or no key)
         return;
@@ -344,8 +352,7 @@ __global__ void __launch_bounds__(D) decode_xchg_kernel(const DecodeParams p, co
     __shared__ int timed_out;
     const uint32_t h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const uint32_t row = b * p.heads + h, par = x.epoch & 1u;
-    const int32_t lraw = p.kv_len ? p.kv_len[b] : int32_t(p.len);
-    const uint32_t L = lraw > 0 ? uint32_t(lraw) : 0u;
+    const uint32_t L = seq_keys(p, b);
     const uint32_t ns = min((L + p.chunk - 1) / p.chunk, p.n_splits);
     const uint64_t row0 = (uint64_t(b) * p.heads + h) * p.n_splits;
     if (d == 0)
@@ -590,7 +597,9 @@ std::mutex g_scratch_mutex;
 void* g_scratch_addr[kMaxDevices] = {};
 
 // The array's device address on `device` (current), looked up once per device.  In host code the array's name is
-// only a host-side stand-in, never a usable device address.
+// only a host-side stand-in, never a usable device address.  The address belongs to the device's primary context:
+// cudaDeviceReset destroys that context, so a process that resets a device must not call the entry point on that
+// device again (the remembered address would be stale).
 int scratch_address(int device, void** out)
 {
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
@@ -636,18 +645,19 @@ extern "C" int mako_attention_decode_noalloc(void* stream, int dtype, const void
     // The split plan of mako_attention_decode, with larger chunks when its partials would not fit the array.
     uint32_t chunk, n_splits;
     mako::decode_plan(max_kv_len, batch, kv_heads, heads, sms, 0, &chunk, &n_splits);
-    // Layout in the array: o partials, then (max, sum) partials.
-    auto bytes_for = [&](uint64_t ns) {
-        return (uint64_t(batch) * heads * ns * dim * 4 + 255) / 256 * 256 + uint64_t(batch) * heads * ns * 8;
-    };
-    if (bytes_for(1) > kNoAllocScratchBytes)
+    // Layout in the array: o partials [batch][heads][n_splits][dim] fp32, then (max, sum) [batch][heads][n_splits].
+    // With dim >= 64 the o block is a whole number of 256-byte lines, so the (max, sum) block needs no padding and a
+    // split of every row costs exactly per_split bytes.
+    const uint64_t per_split = uint64_t(batch) * heads * (uint64_t(dim) * 4 + 8);
+    const uint64_t ns_max = kNoAllocScratchBytes / per_split;  // the most splits a row whose partials fit
+    if (ns_max == 0)
         return set_error(MAKO_EINVAL,
                          "decode_noalloc: %u sequences x %u heads of %u need %llu bytes of partials, beyond the %zu-byte "
                          "static scratch (use mako_attention_decode)",
-                         batch, heads, dim, (unsigned long long)bytes_for(1), kNoAllocScratchBytes);
-    while (bytes_for(n_splits) > kNoAllocScratchBytes) {
-        chunk += 64;
-        n_splits = max_kv_len ? (max_kv_len + chunk - 1) / chunk : 1u;
+                         batch, heads, dim, (unsigned long long)per_split, kNoAllocScratchBytes);
+    if (n_splits > ns_max) {  // the smallest multiple of 64 keys a split that needs no more than ns_max splits
+        chunk = uint32_t(((uint64_t(max_kv_len) + ns_max - 1) / ns_max + 63) / 64 * 64);
+        n_splits = (max_kv_len + chunk - 1) / chunk;
     }
     void* base = nullptr;
     if (int rc = scratch_address(device, &base))
@@ -659,7 +669,7 @@ extern "C" int mako_attention_decode_noalloc(void* stream, int dtype, const void
     p.v = v;
     p.o = o;
     p.kv_len = kv_len;
-    p.len = 0;
+    p.len = max_kv_len;
     p.q_bstride = uint64_t(heads) * dim;
     p.q_hstride = dim;
     p.k_hstride = uint64_t(k_stride) * dim;
@@ -672,7 +682,7 @@ extern "C" int mako_attention_decode_noalloc(void* stream, int dtype, const void
     p.n_splits = n_splits;
     p.scale = 1.0f / sqrtf(float(dim));
     // Every partial the combine reads is written by the same call first, so nothing in the array needs clearing.
-    const size_t o_bytes = (size_t(batch) * heads * n_splits * dim * 4 + 255) / 256 * 256;
+    const size_t o_bytes = size_t(batch) * heads * n_splits * dim * 4;
     p.o_part = static_cast<float*>(base);
     p.ml_part = reinterpret_cast<float2*>(static_cast<unsigned char*>(base) + o_bytes);
     if ((e = mako::launch_decode(p, dtype, int(dim), static_cast<cudaStream_t>(stream))) != cudaSuccess)

@@ -65,7 +65,7 @@ struct DecodeParams {
     float* o_part;  // scratch [batch][heads][n_splits][dim]
     float2* ml_part;  // scratch [batch][heads][n_splits]: (max in log2 units, sum)
     const int32_t* kv_len;  // device [batch] lengths, or null: `len` for every sequence
-    uint32_t len;
+    uint32_t len;           // kv_len null: every sequence's length; else the cap (max_kv_len): no key past it is read
     uint64_t q_bstride, q_hstride, k_bstride, k_hstride, o_bstride;  // in elements
     uint32_t batch, heads, kv_heads, chunk, n_splits;
     float scale;

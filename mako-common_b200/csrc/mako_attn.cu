@@ -380,10 +380,11 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
     p.width = width;
     p.o_type = out_type(ctx, dtype);
     p.scale = 1.0f / sqrtf(float(dim));
-    const bool tc_ok = ctx->cc_major == 10;
-    if (ctx->prefill_kernel == 2 && !tc_ok)
+    // The tcgen05 kernels are the path; the mma.sync kernels run only when asked for (MAKO_OPT_PREFILL_KERNEL 1, the
+    // baseline the tests and benchmarks compare against), never as a silent substitute on another device.
+    if (ctx->prefill_kernel != 1 && ctx->cc_major != 10)
         return fail(MAKO_ENOTSUP, "attention: the tcgen05 kernels need sm_100 (sm_%d)", ctx->cc_major * 10);
-    if (tc_ok && ctx->prefill_kernel != 1) {
+    if (ctx->prefill_kernel != 1) {
         void *v16 = nullptr, *vmax = nullptr, *vinv = nullptr;
         if (dtype == MAKO_BF16) {
             if (int rc = scratch(ctx, "v16", size_t(kv_heads) * k_pad * dim * 2, &v16))
@@ -438,7 +439,7 @@ int mako_attention_decode(mako_attn_ctx* ctx, void* stream, int dtype, const voi
     p.v = v;
     p.o = o;
     p.kv_len = kv_len;
-    p.len = 0;
+    p.len = max_kv_len;
     p.q_bstride = uint64_t(heads) * dim;
     p.q_hstride = dim;
     p.k_hstride = uint64_t(k_stride) * dim;
@@ -529,10 +530,9 @@ int sparse_common(mako_attn_ctx* ctx, void* stream, int dtype, mako::AttnParams&
     p.scale = 1.0f / sqrtf(128.0f);
     p.o_type = out_type(ctx, dtype);
     auto st = static_cast<cudaStream_t>(stream);
-    const bool tc_ok = ctx->cc_major == 10;
-    if (ctx->prefill_kernel == 2 && !tc_ok)
+    if (ctx->prefill_kernel != 1 && ctx->cc_major != 10)
         return fail(MAKO_ENOTSUP, "attention_sparse: the tcgen05 kernel needs sm_100 (sm_%d)", ctx->cc_major * 10);
-    if (tc_ok && ctx->prefill_kernel != 1) {
+    if (ctx->prefill_kernel != 1) {
         void *v16 = nullptr, *vmax = nullptr, *vinv = nullptr;
         if (dtype == MAKO_BF16) {
             if (int rc = scratch(ctx, "v16", size_t(p.kv_heads) * p.k_pad * 128 * 2, &v16))
@@ -824,8 +824,10 @@ mako::XchgParams xchg_params(mako_attn_group* g)
         x.area[r] = static_cast<unsigned char*>(g->peer[r]);
     x.n_ranks = g->n_ranks;
     x.rank = g->rank;
-    if (++g->epoch == 0)  // 0 is the flags' initial value: never a call's number
-        g->epoch = 1;
+    // 0 is the flags' initial value, never a call's number; after 0xFFFFFFFF (odd) comes 2 (even), so consecutive
+    // calls keep alternating halves of the exchange area's parity double buffer across the wrap.
+    if (++g->epoch == 0)
+        g->epoch = 2;
     x.epoch = g->epoch;
     x.rows_cap = g->rows_cap;
     x.err = g->ctx->err;
@@ -1136,6 +1138,7 @@ int mako_attention_decode_kv_sharded(mako_attn_group* g, void* stream, int dtype
     p.v = v;
     p.o = o;
     p.kv_len = kv_len;
+    p.len = max_kv_len;
     p.q_bstride = uint64_t(heads) * dim;
     p.q_hstride = dim;
     p.k_hstride = uint64_t(k_stride) * dim;

@@ -160,6 +160,21 @@ def test_decode_zero_length_gives_zeros(ctx, oracle):
     assert C.within(got, want)[0]
 
 
+@pytest.mark.parametrize("cap", [0, 700, 2500])
+def test_decode_lengths_beyond_max_kv_len(ctx, oracle, cap):
+    """A kv_len entry above max_kv_len is read as max_kv_len: no key past it is read (the split plan covers max_kv_len
+    keys) and every o row is still written -- 0 when max_kv_len is 0."""
+    case = C.decode_case(seed=29, batch=4, heads=8, kv_heads=2, dim=128, lo=300, hi=4000, dtype=0)
+    got = run_decode(ctx, case, max_len=cap)
+    assert not np.any(got == SENTINEL)
+    capped = np.minimum(case["kv_len"], cap).astype(np.int32)
+    want = oracle.decode(0, case["q"], case["k"], case["v"], capped, 8, 2, 128, case["k_stride"])
+    if cap == 0:
+        assert np.all(got == 0.0)
+    ok, stats = C.within(got, want)
+    assert ok, f"cap {cap}: {stats}"
+
+
 def sparse_fixture_run(ctx, oracle, dtype=0, topk=3, local=0, stride=0, kernel=0):
     import torch
     import mako_attn
