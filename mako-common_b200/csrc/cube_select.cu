@@ -4,6 +4,7 @@
 //   cube_pool   (ops.metal:927-939)  mean over a cube's 64 rows (all summed, invalid rows are zero) / cnt[c]
 //   cube_scores (ops.metal:942-955)  sc[h][qc][kc] = qp . kp
 //   cube_topk   (ops.metal:959-1027) the local cubes first, then the largest scores, ties to the smaller index
+//               (here: a bitonic sort of packed (score, index) keys, one CTA per query cube and head)
 //
 // The fp32 arithmetic is pinned to one order so that the selection is reproducible bit for bit (the CPU oracle
 // restates it): a sequential sum over the 64 rows then one IEEE division; per score s += ((q0 k0 + q1 k1) + q2 k2)
@@ -73,69 +74,82 @@ __global__ void __launch_bounds__(256) cube_scores_kernel(const CubeParams p)
     }
 }
 
-// One CTA of 256 per (query cube, head); at most 4096 cubes (the reference's bound).
-__global__ void __launch_bounds__(256) cube_topk_kernel(const CubeParams p)
+// ---- top-k by sorting -------------------------------------------------------------------------------------------
+//
+// The selection rule (what the reference's cube_topk produces, ops.metal:959-1027, and what the oracle restates):
+// the `local` cubes first; then, one pick at a time, the largest score not yet picked, ties to the smaller index;
+// a score of -inf or NaN is never picked, and once nothing above -inf is left every further pick is cube 0.
+// Equivalently: the candidates (scores above -inf, not a local pick) in descending (score, -index) order, then 0s.
+// Here one CTA per (query cube, head) packs each candidate into a 64-bit key -- an order-preserving image of the
+// score above the complemented index, so that the key order is exactly that order and all keys differ -- gives every
+// other entry the key 0 (below any candidate), sorts the row's keys in shared memory with a bitonic network and
+// reads the picks off the front.
+
+constexpr uint32_t kTopkMaxCubes = 4096;  // the reference's bound (runtime.cpp:290)
+constexpr uint32_t kTopkThreads = 256;
+
+// Larger floats map to larger unsigned images; -0 maps as +0, since the selection's `>` treats them as equal.
+__device__ __forceinline__ uint32_t order_image(float f)
 {
-    __shared__ float scores[4096];
-    __shared__ float best_v[8];
-    __shared__ uint32_t best_i[8];
-    __shared__ uint32_t n_local;
-    const uint32_t qc = blockIdx.x, h = blockIdx.y, n = p.n_cubes, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const float* row = p.sc + (uint64_t(h) * n + qc) * n;
-    for (uint32_t i = tid; i < n; i += 256)
-        scores[i] = row[i];
-    const uint32_t k = min(p.topk, n);
-    uint16_t* out = p.sel + (uint64_t(h) * n + qc) * k;
-    __syncthreads();
-    uint32_t it = 0;
-    if (p.local) {
-        if (tid == 0) {
-            const uint32_t picks[3] = {qc, qc >= p.stride ? qc - p.stride : n, qc + p.stride < n ? qc + p.stride : n};
-            uint32_t c = 0;
-            for (uint32_t j = 0; j < p.local && c < k; ++j)
-                if (picks[j] < n) {
-                    out[c++] = uint16_t(picks[j]);
-                    scores[picks[j]] = -INFINITY;
-                }
-            n_local = c;
-        }
-        __syncthreads();
-        it = n_local;
+    const uint32_t b = f == 0.0f ? 0u : __float_as_uint(f);
+    return (b >> 31) ? ~b : (b | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kTopkThreads) cube_topk_kernel(const CubeParams p)
+{
+    __shared__ unsigned long long key[kTopkMaxCubes];
+    const uint32_t qc = blockIdx.x, h = blockIdx.y, n = p.n_cubes, tid = threadIdx.x;
+    const uint32_t k = min(p.topk, n);  // >= 1
+    // The local option's forced entries, in this order: the query cube; with local 3 also the cube `stride` before
+    // it and the cube `stride` after it, each when inside [0, n); no more than k in all (n: none).  Every thread
+    // derives the same list.
+    uint32_t nf = 0, f0 = n, f1 = n, f2 = n;
+    if (p.local >= 1)
+        f0 = qc, nf = 1;
+    if (p.local == 3) {
+        if (qc >= p.stride && nf < k)
+            f1 = qc - p.stride, ++nf;
+        if (qc + p.stride < n && nf < k)
+            f2 = qc + p.stride, ++nf;
     }
-    for (; it < k; ++it) {
-        float v = -INFINITY;
-        uint32_t idx = 0;
-        for (uint32_t i = tid; i < n; i += 256)
-            if (scores[i] > v) {
-                v = scores[i];
-                idx = i;
-            }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (ov > v || (ov == v && oi < idx)) {
-                v = ov;
-                idx = oi;
-            }
+    uint32_t width = 2;  // the sorted length: a power of two covering the row
+    while (width < n)
+        width <<= 1;
+    const float* row = p.sc + (uint64_t(h) * n + qc) * n;
+    for (uint32_t i = tid; i < width; i += kTopkThreads) {
+        unsigned long long kv = 0ull;
+        if (i < n) {
+            const float s = row[i];
+            const bool is_forced = i == f0 || i == f1 || i == f2;
+            if (s > -INFINITY && !is_forced)  // false for NaN too
+                kv = (static_cast<unsigned long long>(order_image(s)) << 32) | (0xFFFFFFFFu - i);
         }
-        if (lane == 0) {
-            best_v[wid] = v;
-            best_i[wid] = idx;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            float bv = best_v[0];
-            uint32_t bi = best_i[0];
-            for (int j = 1; j < 8; ++j)
-                if (best_v[j] > bv || (best_v[j] == bv && best_i[j] < bi)) {
-                    bv = best_v[j];
-                    bi = best_i[j];
+        key[i] = kv;
+    }
+    __syncthreads();
+    // Bitonic sort, descending: blocks of `size` alternate direction until the last merge.
+    for (uint32_t size = 2; size <= width; size <<= 1)
+        for (uint32_t half = size >> 1; half > 0; half >>= 1) {
+            for (uint32_t t = tid; t < width / 2; t += kTopkThreads) {
+                const uint32_t i = 2 * t - (t & (half - 1)), j = i + half;
+                const unsigned long long a = key[i], b = key[j];
+                if ((a < b) == ((i & size) == 0)) {
+                    key[i] = b;
+                    key[j] = a;
                 }
-            out[it] = uint16_t(bi);
-            scores[bi] = -INFINITY;
+            }
+            __syncthreads();
         }
-        __syncthreads();
+    uint16_t* out = p.sel + (uint64_t(h) * n + qc) * k;
+    for (uint32_t i = tid; i < k; i += kTopkThreads) {
+        uint32_t c;
+        if (i < nf)
+            c = i == 0 ? f0 : (i == 1 ? (f1 < n ? f1 : f2) : f2);
+        else {
+            const unsigned long long kv = key[i - nf];
+            c = kv ? 0xFFFFFFFFu - uint32_t(kv) : 0u;
+        }
+        out[i] = uint16_t(c);
     }
     if (tid == 0)
         p.nsel[uint64_t(h) * n + qc] = uint16_t(k);

@@ -260,6 +260,7 @@ void oracle_cube_select(int dtype, const uint16_t* q, const uint16_t* k, uint32_
                     out[uint64_t(c) * D + d] = val;
                 }
         }
+#pragma omp parallel for schedule(static)
         for (uint32_t qc = 0; qc < n_cubes; ++qc)
             for (uint32_t kc = 0; kc < n_cubes; ++kc) {
                 const double* a = &qp[uint64_t(qc) * D];
@@ -285,6 +286,7 @@ void oracle_cube_select(int dtype, const uint16_t* q, const uint16_t* k, uint32_
                 }
                 sc[uint64_t(qc) * n_cubes + kc] = val;
             }
+#pragma omp parallel for schedule(dynamic, 16)
         for (uint32_t qc = 0; qc < n_cubes; ++qc) {
             std::vector<double> s(sc.begin() + uint64_t(qc) * n_cubes, sc.begin() + uint64_t(qc + 1) * n_cubes);
             uint16_t* out = sel + (uint64_t(h) * n_cubes + qc) * kk;

@@ -240,6 +240,59 @@ def test_cube_select_large_bit_exact(ctx, oracle):
         np.testing.assert_array_equal(sel, want)
 
 
+def planted_cubes(seed, n_cubes):
+    """One head of n_cubes full cubes, fp16, N(0, 1) with planted edge cases: key cubes 100, 2000 and n - 1 copies of
+    key cube 5, and 8..10 copies of 7 (tied scores in every row); query cube 3 is -inf in dimension 0 and 0 elsewhere
+    (its scores are +inf or -inf by the sign of the key cube's dimension 0: tied +inf candidates, -inf never picked);
+    query cube 11 is NaN (no candidate: every pick after the local ones is cube 0); cube 9 is empty (cnt 0, zero
+    rows: a row and a column of zero scores, all tied)."""
+    rng = np.random.default_rng(seed)
+    n = n_cubes * 64
+    x = C.normal(rng, (2, 1, n, 128))
+    q, k = x[0], x[1]
+    cube = lambda t, c: t[0, c * 64:(c + 1) * 64]  # noqa: E731
+    for c in (100, 2000, n_cubes - 1):
+        cube(k, c)[:] = cube(k, 5)
+    for c in (8, 9, 10):
+        cube(k, c)[:] = cube(k, 7)
+    cube(q, 3)[:] = 0.0
+    cube(q, 3)[:, 0] = -np.inf
+    cube(q, 11)[:] = np.nan
+    cube(q, 9)[:] = 0.0
+    cube(k, 9)[:] = 0.0
+    cnt = np.full(n_cubes, 64, np.uint32)
+    cnt[9] = 0
+    return oracle_bits(q), oracle_bits(k), cnt
+
+
+def oracle_bits(x):
+    import oracle as O
+    return O.to_bits(x, 0)
+
+
+@pytest.mark.parametrize("local,stride", [(0, 0), (3, 256), (3, 0)], ids=["by-score", "local3", "local3-stride0"])
+def test_cube_topk_at_the_reference_bound(ctx, oracle, local, stride):
+    """4096 cubes (the reference's limit, src/models/runtime.cpp:290) with H3's top-k, ceil(0.15 * 4096) = 615
+    (src/models/h3.cpp:520), and the planted ties, infinities, NaNs and empty cube of planted_cubes: the selection
+    equals the fp32 restatement's repeated argmax bit for bit."""
+    import torch
+    n_cubes, topk = 4096, 615
+    n = n_cubes * 64
+    q, k, cnt = planted_cubes(31, n_cubes)
+    want, want_n, _, _, sc = oracle.cube_select(0, q, k, 1, n, n, n_cubes, cnt, topk, local, stride, mode=1)
+    # the planted cases reach the selection as intended
+    assert np.array_equal(sc[0, :, 5], sc[0, :, 100]) and np.array_equal(sc[0, :, 7], sc[0, :, 10])
+    assert np.any(sc[0, 3] == np.inf) and np.any(sc[0, 3] == -np.inf)
+    assert np.all(np.isnan(sc[0, 11])) and np.all(sc[0, 9] == 0.0)
+    sel_t, nsel_t = ctx.cube_select(dev(q, 0), dev(k, 0), 1, n, n, n_cubes, dev_raw(cnt), topk, local, stride)
+    torch.cuda.synchronize()
+    sel, nsel = sel_t.cpu().numpy().view(np.uint16), nsel_t.cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(nsel, want_n)
+    np.testing.assert_array_equal(sel, want)
+    nf = 0 if not local else 1 + (11 >= stride) + (11 + stride < n_cubes)  # query cube 11's forced entries
+    assert np.all(sel[0, 11, nf:] == 0)  # nothing above -inf: cube 0 repeated
+
+
 @pytest.mark.parametrize("kernel", [0, 1], ids=["auto", "mma"])
 def test_block_sparse_lists(ctx, oracle, kernel):
     """Config 4's mask format (int32 sorted kept-block lists + counts) at a reduced length."""
