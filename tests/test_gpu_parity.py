@@ -262,12 +262,7 @@ def planted_cubes(seed, n_cubes):
     cube(k, 9)[:] = 0.0
     cnt = np.full(n_cubes, 64, np.uint32)
     cnt[9] = 0
-    return oracle_bits(q), oracle_bits(k), cnt
-
-
-def oracle_bits(x):
-    import oracle as O
-    return O.to_bits(x, 0)
+    return oracle_bits(q, 0), oracle_bits(k, 0), cnt
 
 
 @pytest.mark.parametrize("local,stride", [(0, 0), (3, 256), (3, 0)], ids=["by-score", "local3", "local3-stride0"])
