@@ -13,7 +13,8 @@
 //                 fp16; ops.metal:303-316); P goes back into S's TMEM columns as fp16 pairs for the P.V product.
 // TMEM (512 columns): S_A 0-127, S_B 128-255, O_A 256-383, O_B 384-511.  The issue order per key tile is
 // PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1) -- while one tile's softmax runs the tensor core works on the other's.
-// QK_X(j+1) is issued after PV_X(j) completes (it overwrites the P that PV_X(j) reads).
+// QK_X(j+1) overwrites the P that PV_X(j) reads and is issued right behind it: the tensor pipe runs one thread's
+// MMAs in issue order.
 //
 // P.V runs in fp16: for fp16 inputs V is used as it is; for bf16 inputs a pre-pass writes V * 2^k per kv head into
 // an fp16 copy (k puts the head's largest |v| in [2^14, 2^15), exact for every value above 2^-28 of that maximum) and
@@ -190,49 +191,32 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                 umma_commit(s_full(1));
                 umma_commit(k_empty(0));
             }
-            // Per tile X the next P.V and the next Q.K^T: PV_X(j) needs P_X(j) from the softmax and V_j; QK_X(j+1)
-            // needs K_{j+1} and PV_X(j) finished (it overwrites the P that PV_X(j) reads).  Whichever product is
-            // ready is issued, so one tile's wait is filled with the other tile's work.
-            uint32_t pv_next[2] = {0, 0}, qk_next[2] = {1, 1};
-            uint32_t k_ok = 1, v_ok = 0;  // K / V tiles seen landed: [0, k_ok), [0, v_ok)
-            long long idle_since = clock64();
-            while (ok && (pv_next[0] < nb || pv_next[1] < nb)) {
-                bool progressed = false;
+            // Fixed order per key tile j: PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1).  QK_X(j+1) is issued right behind
+            // PV_X(j) without waiting for it: the tensor pipe executes one thread's MMAs in issue order, so P_X(j) is
+            // read before Q.K^T overwrites its columns.  Each commit tracks every MMA issued before it, so when the
+            // softmax sees S_X(j+1) the product PV_X(j) has finished too (its O may be rescaled).
+            for (uint32_t j = 0; j < nb && ok; ++j) {
+                const uint32_t st = j % TNS, j1 = j + 1, st1 = j1 % TNS;
+                ok = mbar_wait(v_full(st), (j / TNS) & 1, WAIT_LIMIT);
 #pragma unroll
-                for (uint32_t x = 0; x < 2; ++x) {
-                    const uint32_t j = pv_next[x];
-                    if (j < nb && qk_next[x] > j) {
-                        if (v_ok == j && mbar_test(v_full(j % TNS), (j / TNS) & 1))
-                            v_ok = j + 1;
-                        if (v_ok > j && mbar_test(p_full(x), j & 1)) {
-                            fence_after();
-                            pv(x, j % TNS, j > 0);
-                            umma_commit(pv_done(x));
-                            pv_next[x] = j + 1;
-                            if (pv_next[x ^ 1] > j)  // both tiles' PV of V_j issued: the stage frees when they finish
-                                umma_commit(v_empty(j % TNS));
-                            progressed = true;
-                        }
-                    }
-                    const uint32_t j1 = qk_next[x];
-                    if (j1 < nb && pv_next[x] == j1) {
-                        if (k_ok == j1 && mbar_test(k_full(j1 % TNS), (j1 / TNS) & 1))
-                            k_ok = j1 + 1;
-                        if (k_ok > j1 && mbar_test(pv_done(x), (j1 - 1) & 1)) {
-                            fence_after();
-                            qk(x, j1 % TNS);
-                            umma_commit(s_full(x));
-                            qk_next[x] = j1 + 1;
-                            if (qk_next[x ^ 1] > j1)
-                                umma_commit(k_empty(j1 % TNS));
-                            progressed = true;
-                        }
+                for (uint32_t x = 0; x < 2 && ok; ++x) {
+                    if (!(ok = mbar_wait(p_full(x), j & 1, WAIT_LIMIT)))
+                        break;
+                    fence_after();
+                    pv(x, st, j > 0);
+                    if (x == 1)
+                        umma_commit(v_empty(st));
+                    if (j1 < nb) {
+                        if (x == 0 && !(ok = mbar_wait(k_full(st1), (j1 / TNS) & 1, WAIT_LIMIT)))
+                            break;
+                        qk(x, st1);
+                        umma_commit(s_full(x));
+                        if (x == 1)
+                            umma_commit(k_empty(st1));
+                    } else {
+                        umma_commit(pv_done(x));  // the tile's last product: its O is final
                     }
                 }
-                if (progressed)
-                    idle_since = clock64();
-                else if (clock64() - idle_since > WAIT_LIMIT)
-                    ok = false;
             }
             if (!ok)
                 atomicExch(p.err, 2);
@@ -312,7 +296,8 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             }
             tmem_st32(tl + colS, pk[0]);
             tmem_st32(tl + colS + 32, pk[1]);
-            // Rescale this tile's O before P.V adds to it (PV_X(j-1) finished before QK_X(j) was issued).
+            // Rescale this tile's O before P.V adds to it (PV_X(j-1) finished before S_X(j) was seen: the commit that
+            // signalled S_X(j) tracks it).
             if (__any_sync(0xffffffffu, resc && j > 0)) {
                 const float g = resc ? f : 1.0f;
 #pragma unroll
@@ -332,7 +317,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             mbar_arrive(p_full(x));
         }
         if (ok && nb > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(pv_done(x), (nb - 1) & 1, WAIT_LIMIT));
+            ok = __all_sync(0xffffffffu, mbar_wait(pv_done(x), 0, WAIT_LIMIT));
             fence_after();
         }
         if (!ok && lane == 0)
