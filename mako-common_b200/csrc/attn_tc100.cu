@@ -64,8 +64,37 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Work item i of n_tiles * heads: tile t = n_tiles - 1 - i / heads (rows [256 t, 256 t + 256)), head h = i % heads.
+// Whatever the mask, a later tile sees at least as many keys, so items come longest first.  A CTA takes one item per
+// round of gridDim.x items, snaking (CTA c takes position c in even rounds and G - 1 - c in odd ones) so that every CTA
+// gets a similar total.
+struct TcItem {
+    uint32_t h, q0, kvh, nb;
+    bool live;  // false: past the last item, or a tile whose rows all lie past n_q
+};
+__device__ __forceinline__ uint32_t item_index(uint32_t round)
+{
+    const uint32_t G = gridDim.x, c = (round & 1) ? G - 1 - blockIdx.x : blockIdx.x;
+    return round * G + c;
+}
+__device__ __forceinline__ TcItem tc_item(const TcParams& p, uint32_t i)
+{
+    TcItem it;
+    const uint32_t tile = p.n_tiles - 1 - i / p.heads;
+    it.h = i % p.heads;
+    it.q0 = tile * 2 * TBM;
+    it.kvh = it.h / (p.heads / p.kv_heads);
+    it.live = it.q0 < p.n_q;
+    const uint32_t last = p.q_pos0 + min(it.q0 + 2 * TBM, p.n_q) - 1;
+    const uint32_t n_keys = last >= p.block ? p.n_k : min(p.n_k, last + 1);
+    it.nb = it.live ? (n_keys + TBN - 1) / TBN : 0;
+    return it;
+}
+
 // TD: head width (64 or 128).  GATHER: the head-sharded form's epilogue (TMA stores into every rank's o, 128-wide
-// heads); otherwise plain stores into p.od[0].
+// heads; launched with one item per CTA, since the epilogue stages its boxes in the Q buffer); otherwise plain
+// stores into p.od[0] and a persistent grid: while the softmax warps store one item's output, the producer already
+// loads the next item's Q and keys and the issuer starts its Q.K^T.
 template <int TD, bool GATHER>
 __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__ TcParams p)
 {
@@ -86,20 +115,15 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
     auto pv_done = [&](uint32_t x) { return sB + 104 + 8 * x; };
     const uint32_t mma_done = sB + 120;
     const uint32_t tmem_slot = sB + 128;
+    const uint32_t q_empty = sB + 136;  // an item's last Q.K^T has finished: Q may be overwritten
     volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t tile = p.n_tiles - 1 - blockIdx.x;  // the longest causal rows first
-    const uint32_t h = blockIdx.y, q0 = tile * 2 * TBM;
-    if (q0 >= p.n_q)
-        return;
-    const uint32_t kvh = h / (p.heads / p.kv_heads);
-    const uint32_t last = p.q_pos0 + min(q0 + 2 * TBM, p.n_q) - 1;
-    const uint32_t n_keys = last >= p.block ? p.n_k : min(p.n_k, last + 1);
-    const uint32_t nb = (n_keys + TBN - 1) / TBN;
+    const uint32_t n_items = p.n_tiles * p.heads;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         for (uint32_t s = 0; s < TNS; ++s) {
             mbar_init(k_full(s), 1);
             mbar_init(k_empty(s), 1);
@@ -123,49 +147,70 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
     fence_after();
     const uint32_t tmem = *tmem_slot_ptr;
 
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
+    // Counters every role keeps alike: g counts the key tiles of the items so far (K / V ring stages, and the phases
+    // of s_full / p_full), nq the items with Q loaded, nk the items with at least one key tile (pv_done phases).
+    if (warp < 4) {
+        // the producer and issuer warpgroup gives registers to the softmax warpgroups (384 x 168 at launch =
+        // 128 x 104 + 256 x 200)
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 104;\n" ::: "memory");
+        if (warp == 0 && lane == 0) {
+            // ---------------- TMA producer ----------------
             tma_prefetch_desc(&p.tq);
             tma_prefetch_desc(&p.tk);
             tma_prefetch_desc(&p.tv);
             bool ok = true;
-            mbar_expect_tx(q_full, 2 * TILE_BYTES);
-            for (int x = 0; x < 2; ++x)
-                for (int half = 0; half < TD / 64; ++half)
-                    tma_load_3d(sQ + x * TILE_BYTES + half * BOX_BYTES, &p.tq, q_full, half * 64, q0 + x * TBM, h);
-            uint32_t issued = 0;
-            for (uint32_t j = 0; j < nb && ok; ++j) {
-                const uint32_t s = j % TNS, ph = (j / TNS) & 1;
-                if (j >= TNS && !mbar_wait(k_empty(s), ph ^ 1, WAIT_LIMIT)) {
+            uint32_t g = 0, nq = 0, issued = 0;  // issued: K / V loads so far (2 per key tile)
+            for (uint32_t round = 0; ok; ++round) {
+                const uint32_t i = item_index(round);
+                if (i >= n_items)
+                    break;
+                const TcItem it = tc_item(p, i);
+                if (!it.live)
+                    continue;
+                if (nq > 0 && !mbar_wait(q_empty, (nq - 1) & 1, WAIT_LIMIT)) {
                     ok = false;
                     break;
                 }
-                mbar_expect_tx(k_full(s), TILE_BYTES);
-                for (int half = 0; half < TD / 64; ++half)
-                    tma_load_3d(sK + s * TILE_BYTES + half * BOX_BYTES, &p.tk, k_full(s), half * 64, j * TBN, kvh);
-                if (j >= TNS && !mbar_wait(v_empty(s), ph ^ 1, WAIT_LIMIT)) {
-                    ok = false;
-                    issued = 2 * j + 1;
-                    break;
+                mbar_expect_tx(q_full, 2 * TILE_BYTES);
+                for (int x = 0; x < 2; ++x)
+                    for (int half = 0; half < TD / 64; ++half)
+                        tma_load_3d(sQ + x * TILE_BYTES + half * BOX_BYTES, &p.tq, q_full, half * 64,
+                                    it.q0 + x * TBM, it.h);
+                ++nq;
+                for (uint32_t j = 0; j < it.nb; ++j) {
+                    const uint32_t gj = g + j, s = gj % TNS, ph = (gj / TNS) & 1;
+                    if (gj >= TNS && !mbar_wait(k_empty(s), ph ^ 1, WAIT_LIMIT)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(k_full(s), TILE_BYTES);
+                    for (int half = 0; half < TD / 64; ++half)
+                        tma_load_3d(sK + s * TILE_BYTES + half * BOX_BYTES, &p.tk, k_full(s), half * 64, j * TBN,
+                                    it.kvh);
+                    ++issued;
+                    if (gj >= TNS && !mbar_wait(v_empty(s), ph ^ 1, WAIT_LIMIT)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(v_full(s), TILE_BYTES);
+                    for (int half = 0; half < TD / 64; ++half)
+                        tma_load_3d(sV + s * TILE_BYTES + half * BOX_BYTES, &p.tv, v_full(s), half * 64, j * TBN,
+                                    it.kvh);
+                    ++issued;
                 }
-                mbar_expect_tx(v_full(s), TILE_BYTES);
-                for (int half = 0; half < TD / 64; ++half)
-                    tma_load_3d(sV + s * TILE_BYTES + half * BOX_BYTES, &p.tv, v_full(s), half * 64, j * TBN, kvh);
-                issued = 2 * (j + 1);
+                g += it.nb;
             }
             if (!ok)
                 atomicExch(p.err, 1);
             // Our copies in flight land before the CTA leaves (already so on the normal path).
-            mbar_wait(q_full, 0, WAIT_LIMIT);
-            for (uint32_t i = issued > 2 * TNS ? issued - 2 * TNS : 0; i < issued; ++i) {
-                const uint32_t j = i / 2, s = j % TNS, ph = (j / TNS) & 1;
-                mbar_wait((i & 1) ? v_full(s) : k_full(s), ph, WAIT_LIMIT);
+            if (nq > 0)
+                mbar_wait(q_full, (nq - 1) & 1, WAIT_LIMIT);
+            for (uint32_t k = issued > 2 * TNS ? issued - 2 * TNS : 0; k < issued; ++k) {
+                const uint32_t gj = k / 2, s = gj % TNS, ph = (gj / TNS) & 1;
+                mbar_wait((k & 1) ? v_full(s) : k_full(s), ph, WAIT_LIMIT);
             }
-        }
-    } else if (warp == 1) {
-        // ---------------- UMMA issuer ----------------
-        if (lane == 0 && nb > 0) {
+        } else if (warp == 1 && lane == 0) {
+            // ---------------- UMMA issuer ----------------
             const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, TBM, TBN);
             const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, TBM, TD);
             auto qk = [&](uint32_t x, uint32_t stage) {
@@ -182,206 +227,245 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                     umma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
                             sdesc(sV + stage * TILE_BYTES + kk * 2048, BOX_BYTES, 1024), idesc_pv, acc || kk > 0);
             };
-            bool ok = mbar_wait(q_full, 0, WAIT_LIMIT) && mbar_wait(k_full(0), 0, WAIT_LIMIT);
-            if (ok) {
+            bool ok = true;
+            uint32_t g = 0, nq = 0;
+            for (uint32_t round = 0; ok; ++round) {
+                const uint32_t i = item_index(round);
+                if (i >= n_items)
+                    break;
+                const TcItem it = tc_item(p, i);
+                if (!it.live)
+                    continue;
+                if (!(ok = mbar_wait(q_full, nq & 1, WAIT_LIMIT)))
+                    break;
+                ++nq;
+                if (it.nb == 0) {
+                    umma_commit(q_empty);
+                    continue;
+                }
+                if (!(ok = mbar_wait(k_full(g % TNS), (g / TNS) & 1, WAIT_LIMIT)))
+                    break;
                 fence_after();
-                qk(0, 0);
+                qk(0, g % TNS);
                 umma_commit(s_full(0));
-                qk(1, 0);
+                qk(1, g % TNS);
                 umma_commit(s_full(1));
-                umma_commit(k_empty(0));
-            }
-            // Fixed order per key tile j: PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1).  QK_X(j+1) is issued right behind
-            // PV_X(j) without waiting for it: the tensor pipe executes one thread's MMAs in issue order, so P_X(j) is
-            // read before Q.K^T overwrites its columns.  Each commit tracks every MMA issued before it, so when the
-            // softmax sees S_X(j+1) the product PV_X(j) has finished too (its O may be rescaled).
-            for (uint32_t j = 0; j < nb && ok; ++j) {
-                const uint32_t st = j % TNS, j1 = j + 1, st1 = j1 % TNS;
-                ok = mbar_wait(v_full(st), (j / TNS) & 1, WAIT_LIMIT);
+                umma_commit(k_empty(g % TNS));
+                if (it.nb == 1)
+                    umma_commit(q_empty);
+                // Fixed order per key tile j: PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1).  QK_X(j+1) is issued right
+                // behind PV_X(j) without waiting for it: the tensor pipe executes one thread's MMAs in issue order, so
+                // P_X(j) is read before Q.K^T overwrites its columns.  Each commit tracks every MMA issued before it,
+                // so when the softmax sees S_X(j+1) the product PV_X(j) has finished too (its O may be rescaled).
+                // An item's first Q.K^T follows the previous item's last P.V the same way.
+                for (uint32_t j = 0; j < it.nb && ok; ++j) {
+                    const uint32_t gj = g + j, st = gj % TNS, g1 = gj + 1, st1 = g1 % TNS;
+                    ok = mbar_wait(v_full(st), (gj / TNS) & 1, WAIT_LIMIT);
 #pragma unroll
-                for (uint32_t x = 0; x < 2 && ok; ++x) {
-                    if (!(ok = mbar_wait(p_full(x), j & 1, WAIT_LIMIT)))
-                        break;
-                    fence_after();
-                    pv(x, st, j > 0);
-                    if (x == 1)
-                        umma_commit(v_empty(st));
-                    if (j1 < nb) {
-                        if (x == 0 && !(ok = mbar_wait(k_full(st1), (j1 / TNS) & 1, WAIT_LIMIT)))
+                    for (uint32_t x = 0; x < 2 && ok; ++x) {
+                        if (!(ok = mbar_wait(p_full(x), gj & 1, WAIT_LIMIT)))
                             break;
-                        qk(x, st1);
-                        umma_commit(s_full(x));
+                        fence_after();
+                        pv(x, st, j > 0);
                         if (x == 1)
-                            umma_commit(k_empty(st1));
-                    } else {
-                        umma_commit(pv_done(x));  // the tile's last product: its O is final
+                            umma_commit(v_empty(st));
+                        if (j + 1 < it.nb) {
+                            if (x == 0 && !(ok = mbar_wait(k_full(st1), (g1 / TNS) & 1, WAIT_LIMIT)))
+                                break;
+                            qk(x, st1);
+                            umma_commit(s_full(x));
+                            if (x == 1) {
+                                umma_commit(k_empty(st1));
+                                if (j + 2 == it.nb)
+                                    umma_commit(q_empty);
+                            }
+                        } else {
+                            umma_commit(pv_done(x));  // the tile's last product: its O is final
+                        }
                     }
                 }
+                g += it.nb;
             }
             if (!ok)
                 atomicExch(p.err, 2);
             umma_commit(mma_done);  // every MMA issued above has finished before TMEM is freed
             mbar_wait(mma_done, 0, WAIT_LIMIT);
         }
-    } else if (warp >= 4) {
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
         // ---------------- softmax (and epilogue) of tile X ----------------
         const uint32_t x = (warp - 4) >> 2, ql = (warp & 3) * 32, row = ql + lane;
         const uint32_t tl = tmem + (ql << 16);
         const uint32_t colS = x * 128, colO = 256 + x * 128;
-        const uint32_t pos = p.q_pos0 + q0 + x * TBM + row;
-        const uint32_t lim = pos >= p.block ? p.n_k : min(p.n_k, pos + 1);  // this row sees keys [0, lim)
-        const uint32_t pos1 = p.q_pos0 + q0 + x * TBM;
-        const uint32_t lim1 = pos1 >= p.block ? p.n_k : min(p.n_k, pos1 + 1);  // the tile's first row
         const float scale = p.scale_log2;
-        float m = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (uint32_t j = 0; j < nb; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), j & 1, WAIT_LIMIT));
-            if (!ok)
+        uint32_t g = 0, nk = 0;
+        for (uint32_t round = 0; ok; ++round) {
+            const uint32_t i = item_index(round);
+            if (i >= n_items)
                 break;
-            fence_after();
-            uint32_t r[4][32];
+            const TcItem it = tc_item(p, i);
+            if (!it.live)
+                continue;
+            const uint32_t h = it.h, q0 = it.q0, nb = it.nb;
+            const uint32_t pos = p.q_pos0 + q0 + x * TBM + row;
+            const uint32_t lim = pos >= p.block ? p.n_k : min(p.n_k, pos + 1);  // this row sees keys [0, lim)
+            const uint32_t pos1 = p.q_pos0 + q0 + x * TBM;
+            const uint32_t lim1 = pos1 >= p.block ? p.n_k : min(p.n_k, pos1 + 1);  // the tile's first row
+            float m = -INFINITY, l = 0.0f;
+            for (uint32_t j = 0; j < nb; ++j) {
+                ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), (g + j) & 1, WAIT_LIMIT));
+                if (!ok)
+                    break;
+                fence_after();
+                uint32_t r[4][32];
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                tmem_ld32(tl + colS + c * 32, r[c]);
-            tmem_wait_ld();
+                for (int c = 0; c < 4; ++c)
+                    tmem_ld32(tl + colS + c * 32, r[c]);
+                tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                reg_fence(r[c]);
-            const uint32_t j0 = j * TBN;
-            if (j0 + TBN > lim1) {  // a tile the mask cuts: keys at or past this row's limit drop out
+                for (int c = 0; c < 4; ++c)
+                    reg_fence(r[c]);
+                const uint32_t j0 = j * TBN;
+                if (j0 + TBN > lim1) {  // a tile the mask cuts: keys at or past this row's limit drop out
 #pragma unroll
-                for (int c = 0; c < TBN; ++c)
-                    if (j0 + c >= lim)
-                        r[c >> 5][c & 31] = 0xFF800000u;  // -inf
+                    for (int c = 0; c < TBN; ++c)
+                        if (j0 + c >= lim)
+                            r[c >> 5][c & 31] = 0xFF800000u;  // -inf
+                }
+                // Row maximum of the raw scores (scale > 0 keeps the order), three at a time, four chains.
+                float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int c = 0; c < TBN; c += 8)
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        mq[t] = max3f(mq[t], __uint_as_float(r[(c + 2 * t) >> 5][(c + 2 * t) & 31]),
+                                      __uint_as_float(r[(c + 2 * t + 1) >> 5][(c + 2 * t + 1) & 31]));
+                const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
+                float f = 1.0f;
+                bool resc = false;
+                if (mx > m + 8.0f) {
+                    f = m == -INFINITY ? 0.0f : ex2(m - mx);
+                    m = mx;
+                    l *= f;
+                    resc = true;
+                }
+                // P = 2^(s * scale - m), two lanes per FMA; a row with no visible key so far has every s = -inf.
+                const float mneg = m == -INFINITY ? 0.0f : -m;
+                const uint64_t scale2 = pack2(scale, scale), mneg2 = pack2(mneg, mneg);
+                uint32_t pk[2][32];
+                uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
+#pragma unroll
+                for (int c = 0; c < TBN / 2; ++c) {
+                    const uint64_t s2 = pack2(__uint_as_float(r[(2 * c) >> 5][(2 * c) & 31]),
+                                              __uint_as_float(r[(2 * c + 1) >> 5][(2 * c + 1) & 31]));
+                    float a, b;
+                    unpack2(ffma2(s2, scale2, mneg2), a, b);
+                    a = ex2(a);
+                    b = ex2(b);
+                    sum2[c & 1] = fadd2(sum2[c & 1], pack2(a, b));
+                    pk[c >> 5][c & 31] = pack_half2(a, b);
+                }
+                {
+                    float s0, s1, s2, s3;
+                    unpack2(sum2[0], s0, s1);
+                    unpack2(sum2[1], s2, s3);
+                    l += (s0 + s1) + (s2 + s3);
+                }
+                tmem_st32(tl + colS, pk[0]);
+                tmem_st32(tl + colS + 32, pk[1]);
+                // Rescale this tile's O before P.V adds to it (PV_X(j-1) finished before S_X(j) was seen: the commit
+                // that signalled S_X(j) tracks it).
+                if (__any_sync(0xffffffffu, resc && j > 0)) {
+                    const float gsc = resc ? f : 1.0f;
+#pragma unroll
+                    for (int c = 0; c < TD / 32; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(tl + colO + c * 32, o);
+                        tmem_wait_ld();
+                        reg_fence(o);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * gsc);
+                        tmem_st32(tl + colO + c * 32, o);
+                    }
+                }
+                tmem_wait_st();
+                fence_before();
+                mbar_arrive(p_full(x));
             }
-            // Row maximum of the raw scores (scale > 0 keeps the order), three at a time, four chains.
-            float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int c = 0; c < TBN; c += 8)
-#pragma unroll
-                for (int t = 0; t < 4; ++t)
-                    mq[t] = max3f(mq[t], __uint_as_float(r[(c + 2 * t) >> 5][(c + 2 * t) & 31]),
-                                  __uint_as_float(r[(c + 2 * t + 1) >> 5][(c + 2 * t + 1) & 31]));
-            const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
-            float f = 1.0f;
-            bool resc = false;
-            if (mx > m + 8.0f) {
-                f = m == -INFINITY ? 0.0f : ex2(m - mx);
-                m = mx;
-                l *= f;
-                resc = true;
+            if (ok && nb > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(pv_done(x), nk & 1, WAIT_LIMIT));
+                fence_after();
             }
-            // P = 2^(s * scale - m), two lanes per FMA; a row with no visible key so far has every s = -inf.
-            const float mneg = m == -INFINITY ? 0.0f : -m;
-            const uint64_t scale2 = pack2(scale, scale), mneg2 = pack2(mneg, mneg);
-            uint32_t pk[2][32];
-            uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
+            nk += nb > 0;
+            g += nb;
+            const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[it.kvh] : 1.0f);
+            const uint32_t grow = q0 + x * TBM + row;
+            if (GATHER) {
+                // Head-sharded form: the tile's output goes through its Q buffer (free since its last Q.K^T) as
+                // 128-byte swizzled boxes of 128 rows x 32 floats, and TMA stores each box into every rank's o.  The
+                // stores run asynchronously -- the next CTA on this SM computes while they cross NVLink.  Two halves
+                // of 64 columns.
+                const uint32_t stage = sQ + x * TILE_BYTES;
 #pragma unroll
-            for (int c = 0; c < TBN / 2; ++c) {
-                const uint64_t x = pack2(__uint_as_float(r[(2 * c) >> 5][(2 * c) & 31]),
-                                         __uint_as_float(r[(2 * c + 1) >> 5][(2 * c + 1) & 31]));
-                float a, b;
-                unpack2(ffma2(x, scale2, mneg2), a, b);
-                a = ex2(a);
-                b = ex2(b);
-                sum2[c & 1] = fadd2(sum2[c & 1], pack2(a, b));
-                pk[c >> 5][c & 31] = pack_half2(a, b);
-            }
-            {
-                float s0, s1, s2, s3;
-                unpack2(sum2[0], s0, s1);
-                unpack2(sum2[1], s2, s3);
-                l += (s0 + s1) + (s2 + s3);
-            }
-            tmem_st32(tl + colS, pk[0]);
-            tmem_st32(tl + colS + 32, pk[1]);
-            // Rescale this tile's O before P.V adds to it (PV_X(j-1) finished before S_X(j) was seen: the commit that
-            // signalled S_X(j) tracks it).
-            if (__any_sync(0xffffffffu, resc && j > 0)) {
-                const float g = resc ? f : 1.0f;
+                for (int half = 0; half < TD / 64; ++half) {
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc) {
+                        uint32_t o[32];
+                        if (ok && nb > 0) {
+                            tmem_ld32(tl + colO + (2 * half + cc) * 32, o);
+                            tmem_wait_ld();
+                            reg_fence(o);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e)
+                                o[e] = 0u;
+                        }
+                        const uint32_t rbase = stage + cc * BOX_BYTES + row * 128;
+#pragma unroll
+                        for (int k = 0; k < 8; ++k)
+                            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(rbase +
+                                                                                            ((k ^ (row & 7)) * 16)),
+                                         "f"(__uint_as_float(o[4 * k]) * inv), "f"(__uint_as_float(o[4 * k + 1]) * inv),
+                                         "f"(__uint_as_float(o[4 * k + 2]) * inv),
+                                         "f"(__uint_as_float(o[4 * k + 3]) * inv)
+                                         : "memory");
+                    }
+                    fence_proxy_async_smem();
+                    named_bar(1 + x, 128);
+                    if (row == 0) {
+                        for (uint32_t dI = 0; dI < p.n_od; ++dI)
+#pragma unroll
+                            for (int cc = 0; cc < 2; ++cc)
+                                tma_store_2d(&p.to[dI], stage + cc * BOX_BYTES,
+                                             int((p.head0 + h) * TD + (2 * half + cc) * 32), int(q0 + x * TBM));
+                        bulk_commit();
+                        bulk_wait_read0();  // the staging buffer may be rewritten
+                    }
+                    named_bar(1 + x, 128);
+                }
+            } else {
+                const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(h) * TD;
 #pragma unroll
                 for (int c = 0; c < TD / 32; ++c) {
                     uint32_t o[32];
-                    tmem_ld32(tl + colO + c * 32, o);
-                    tmem_wait_ld();
-                    reg_fence(o);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        o[i] = __float_as_uint(__uint_as_float(o[i]) * g);
-                    tmem_st32(tl + colO + c * 32, o);
-                }
-            }
-            tmem_wait_st();
-            fence_before();
-            mbar_arrive(p_full(x));
-        }
-        if (ok && nb > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(pv_done(x), 0, WAIT_LIMIT));
-            fence_after();
-        }
-        if (!ok && lane == 0)
-            atomicExch(p.err, 3);
-        const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
-        const uint32_t grow = q0 + x * TBM + row;
-        if (GATHER) {
-            // Head-sharded form: the tile's output goes through its Q buffer (free since its last Q.K^T) as 128-byte
-            // swizzled boxes of 128 rows x 32 floats, and TMA stores each box into every rank's o.  The stores run
-            // asynchronously -- the next CTA on this SM computes while they cross NVLink.  Two halves of 64 columns.
-            const uint32_t stage = sQ + x * TILE_BYTES;
-#pragma unroll
-            for (int half = 0; half < TD / 64; ++half) {
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    uint32_t o[32];
                     if (ok && nb > 0) {
-                        tmem_ld32(tl + colO + (2 * half + cc) * 32, o);
+                        tmem_ld32(tl + colO + c * 32, o);
                         tmem_wait_ld();
                         reg_fence(o);
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            o[i] = 0u;
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = 0u;
                     }
-                    const uint32_t rbase = stage + cc * BOX_BYTES + row * 128;
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(rbase + ((k ^ (row & 7)) * 16)),
-                                     "f"(__uint_as_float(o[4 * k]) * inv), "f"(__uint_as_float(o[4 * k + 1]) * inv),
-                                     "f"(__uint_as_float(o[4 * k + 2]) * inv), "f"(__uint_as_float(o[4 * k + 3]) * inv)
-                                     : "memory");
+                    if (grow < p.n_q)
+                        out_store32(p.od[0], ooff + c * 32, o, inv, p.o_type);
                 }
-                fence_proxy_async_smem();
-                named_bar(1 + x, 128);
-                if (row == 0) {
-                    for (uint32_t dI = 0; dI < p.n_od; ++dI)
-#pragma unroll
-                        for (int cc = 0; cc < 2; ++cc)
-                            tma_store_2d(&p.to[dI], stage + cc * BOX_BYTES,
-                                         int((p.head0 + h) * TD + (2 * half + cc) * 32), int(q0 + x * TBM));
-                    bulk_commit();
-                    bulk_wait_read0();  // the staging buffer may be rewritten
-                }
-                named_bar(1 + x, 128);
             }
-        } else {
-        const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(h) * TD;
-#pragma unroll
-        for (int c = 0; c < TD / 32; ++c) {
-            uint32_t o[32];
-            if (ok && nb > 0) {
-                tmem_ld32(tl + colO + c * 32, o);
-                tmem_wait_ld();
-                reg_fence(o);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    o[i] = 0u;
-            }
-            if (grow < p.n_q)
-                out_store32(p.od[0], ooff + c * 32, o, inv, p.o_type);
         }
-        }
+        if (!ok && lane == 0)
+            atomicExch(p.err, 3);
     }
     __syncwarp();
     fence_before();
@@ -554,7 +638,12 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, int dim, const void* 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess)
         return e;
-    kern<<<dim3(p.n_tiles, a.heads), TNT, smem, st>>>(p);
+    // One item per CTA for the head-sharded form (its epilogue stages in the Q buffer); otherwise one CTA per SM,
+    // each working through its share of the items.
+    const uint32_t n_items = p.n_tiles * a.heads;
+    const uint32_t sms = a.num_sms ? a.num_sms : 148;
+    const uint32_t grid = gather ? n_items : (n_items < sms ? n_items : sms);
+    kern<<<grid, TNT, smem, st>>>(p);
     return cudaGetLastError();
 }
 

@@ -33,6 +33,7 @@ struct AttnParams {
     float* od[8];
     uint32_t n_od, head0;
     uint32_t o_type;  // element type of o: 0 fp32, 1 fp16, 2 bf16 (single-destination forms)
+    uint32_t num_sms;  // SMs of the device (the persistent kernels' grid); 0: 148
 };
 
 // Portable flash attention on mma.sync tensor cores, any head width of 64 / 128 / 256.

@@ -365,6 +365,7 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
         return launched("attention (decode combine)", mako::launch_decode_combine(p, int(dim), st));
     }
     mako::AttnParams p{};
+    p.num_sms = uint32_t(ctx->num_sms);
     p.q = q;
     p.k = k;
     p.v = v;
@@ -586,6 +587,7 @@ int mako_attention_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const voi
     if (n_q == 0)
         return MAKO_OK;
     mako::AttnParams p{};
+    p.num_sms = uint32_t(ctx->num_sms);
     p.q = q;
     p.k = k;
     p.v = v;
@@ -622,6 +624,7 @@ int mako_attention_block_sparse(mako_attn_ctx* ctx, void* stream, int dtype, con
     if (n == 0)
         return MAKO_OK;
     mako::AttnParams p{};
+    p.num_sms = uint32_t(ctx->num_sms);
     p.q = q;
     p.k = k;
     p.v = v;
@@ -1059,6 +1062,7 @@ int mako_attention_gather(mako_attn_group* g, void* stream, int dtype, const voi
         return cuda_fail("set device", dg.err);
     auto st = static_cast<cudaStream_t>(stream);
     mako::AttnParams p{};
+    p.num_sms = uint32_t(ctx->num_sms);
     p.q = q;
     p.k = k;
     p.v = v;
