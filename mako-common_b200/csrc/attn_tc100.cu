@@ -55,6 +55,7 @@ struct __align__(64) TcParams {
     const float* vinv;  // per kv head: 1 / (the fp16 copy's scale), null for fp16 inputs
     uint32_t qk_fmt;    // Q / K element format: 0 fp16, 1 bf16
     uint32_t n_q, q_pad, n_k, k_pad, heads, kv_heads, q_pos0, block, width, n_tiles;
+    uint32_t group_heads;  // heads per group of the work order (a multiple of heads / kv_heads)
     float scale_log2;
 };
 
@@ -64,10 +65,11 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Work item i of n_tiles * heads: tile t = n_tiles - 1 - i / heads (rows [256 t, 256 t + 256)), head h = i % heads.
-// Whatever the mask, a later tile sees at least as many keys, so items come longest first.  A CTA takes one item per
-// round of gridDim.x items, snaking (CTA c takes position c in even rounds and G - 1 - c in odd ones) so that every CTA
-// gets a similar total.
+// Work items: the heads in groups of group_heads whose keys and values fit in about half the L2 (all heads when they
+// do), group after group; within a group, tile t = n_tiles - 1 down to 0 (rows [256 t, 256 t + 256)), each over the
+// group's heads.  Whatever the mask, a later tile sees at least as many keys, so a group's items come longest first,
+// while the CTAs in flight read the keys of one group only.  A CTA takes one item per round of gridDim.x items,
+// snaking (CTA c takes position c in even rounds and G - 1 - c in odd ones) so that every CTA gets a similar total.
 struct TcItem {
     uint32_t h, q0, kvh, nb;
     bool live;  // false: past the last item, or a tile whose rows all lie past n_q
@@ -80,8 +82,10 @@ __device__ __forceinline__ uint32_t item_index(uint32_t round)
 __device__ __forceinline__ TcItem tc_item(const TcParams& p, uint32_t i)
 {
     TcItem it;
-    const uint32_t tile = p.n_tiles - 1 - i / p.heads;
-    it.h = i % p.heads;
+    const uint32_t per_group = p.group_heads * p.n_tiles, grp = i / per_group, k = i % per_group;
+    const uint32_t gh = min(p.group_heads, p.heads - grp * p.group_heads);  // heads in this group
+    const uint32_t tile = p.n_tiles - 1 - k / gh;
+    it.h = grp * p.group_heads + k % gh;
     it.q0 = tile * 2 * TBM;
     it.kvh = it.h / (p.heads / p.kv_heads);
     it.live = it.q0 < p.n_q;
@@ -629,6 +633,13 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, int dim, const void* 
     p.block = a.block;
     p.width = a.width;
     p.n_tiles = (a.q_pad + 2 * TBM - 1) / (2 * TBM);
+    {
+        // kv heads whose keys and values take at most 64 MB (about half the 126 MB L2), at least one
+        const uint64_t kv_bytes = uint64_t(a.n_k) * dim * 2 * 2;
+        uint64_t kv_per_group = kv_bytes ? (uint64_t(64) << 20) / kv_bytes : a.kv_heads;
+        kv_per_group = kv_per_group < 1 ? 1 : (kv_per_group > a.kv_heads ? a.kv_heads : kv_per_group);
+        p.group_heads = uint32_t(kv_per_group) * (a.heads / a.kv_heads);
+    }
     p.scale_log2 = a.scale * kLog2e;
     const bool gather = p.n_od > 1;
     if (gather && dim != 128)

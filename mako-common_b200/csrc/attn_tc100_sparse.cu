@@ -158,6 +158,17 @@ __device__ __forceinline__ void mask_keys(uint32_t (&r)[NC], const uint8_t* vali
     }
 }
 
+// Work item i of tiles_total * heads: head h = i / tiles_total, row tile u = tiles_total - 1 - i % tiles_total (the
+// tiles after the cubes, which see every key, first).  Consecutive items share a head, so the CTAs in flight read the
+// keys of a few heads and those stay in L2.  A persistent CTA takes one item per round of gridDim.x items, snaking as the
+// dense kernel does; while the softmax warps store one item's output, the producers load the next item's Q and first
+// key cubes and the issuer starts its Q.K^T.
+__device__ __forceinline__ uint32_t sp_item(uint32_t round)
+{
+    const uint32_t G = gridDim.x, c = (round & 1) ? G - 1 - blockIdx.x : blockIdx.x;
+    return round * G + c;
+}
+
 __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_constant__ SpParams p)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -174,12 +185,17 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     auto p_full = [&](uint32_t b) { return sB + 128 + 8 * b; };
     const uint32_t pv_done = sB + 144, q_full = sB + 152, mma_done = sB + 160;
     const uint32_t tmem_slot = sB + 168;
+    const uint32_t q_empty = sB + 176;  // an item's last Q.K^T has finished: Q may be overwritten
+    const uint32_t o_done = sB + 184;   // an item's last P.V has finished: O is final
     volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t h = blockIdx.y, kvh = h / (p.heads / p.kv_heads);
-    const uint32_t u = gridDim.x - 1 - blockIdx.x;  // the row tiles after the cubes (all keys) first
-    const TileInfo t = tile_info(p, u, h);
+    const uint32_t n_items = p.tiles_total * p.heads;
+    auto item = [&](uint32_t i, uint32_t& h, uint32_t& kvh) {
+        h = i / p.tiles_total;
+        kvh = h / (p.heads / p.kv_heads);
+        return tile_info(p, p.tiles_total - 1 - i % p.tiles_total, h);
+    };
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < 3; ++s) {
@@ -196,6 +212,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         mbar_init(p_full(1), 256);
         mbar_init(pv_done, 1);
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        mbar_init(o_done, 1);
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
@@ -208,64 +226,84 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     fence_after();
     const uint32_t tmem = *tmem_slot_ptr;
 
-    if ((warp == 0 || warp == 2) && lane == 0) {
-        // ---------------- TMA producers: warp 0 the K ring, warp 2 the V ring ----------------
-        if (t.np > 0) {
+    // Counters every role keeps alike: g counts the passes of the items so far (ring stages, S / P buffers and the
+    // phases of their barriers), nq the items with passes (Q loads, q_empty and o_done phases).
+    if (warp < 4) {
+        // the producer / issuer warpgroup gives registers to the softmax warpgroups (384 x 168 at launch =
+        // 128 x 104 + 256 x 200)
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 104;\n" ::: "memory");
+        if ((warp == 0 || warp == 2) && lane == 0) {
+            // ---------------- TMA producers: warp 0 Q and the K ring, warp 2 the V ring ----------------
             const bool is_k = warp == 0;
             const CUtensorMap* map = is_k ? &p.tk : &p.tv;
             const uint32_t ring = base + (is_k ? S_K : S_V), nst = is_k ? NSK : NSV;
             tma_prefetch_desc(map);
-            if (is_k) {  // the tile's Q, once
+            if (is_k)
                 tma_prefetch_desc(&p.tq);
-                mbar_expect_tx(q_full, STILE);
-                for (int dh = 0; dh < 2; ++dh)
-                    tma_load_3d(base + S_Q + dh * DBOX, &p.tq, q_full, dh * 64, int(t.row0), int(h));
-            }
             bool ok = true;
-            uint32_t issued = 0;
-            uint32_t rawn[2] = {raw_entry(p, t, h, 0, 0), raw_entry(p, t, h, 0, 1)};
-            for (uint32_t i = 0; i < t.np; ++i) {
-                uint32_t j0[2], hi;
-                keys_of(p, t, i, 0, rawn[0], j0[0], hi);
-                keys_of(p, t, i, 1, rawn[1], j0[1], hi);
-                if (i + 1 < t.np) {  // the next pass's list entries are read while this pass waits for its stage
-                    rawn[0] = raw_entry(p, t, h, i + 1, 0);
-                    rawn[1] = raw_entry(p, t, h, i + 1, 1);
-                }
-                const uint32_t s = i % nst, ph = (i / nst) & 1;
-                if (i >= nst && !mbar_wait(is_k ? k_empty(s) : v_empty(s), ph ^ 1, S_WAIT_LIMIT)) {
-                    ok = false;
+            uint32_t g = 0, nq = 0, issued = 0;
+            for (uint32_t round = 0; ok; ++round) {
+                const uint32_t i = sp_item(round);
+                if (i >= n_items)
                     break;
-                }
-                const uint32_t full = is_k ? k_full(s) : v_full(s);
-                mbar_expect_tx(full, STILE);
-                for (uint32_t hh = 0; hh < 2; ++hh)
+                uint32_t h, kvh;
+                const TileInfo t = item(i, h, kvh);
+                if (t.np == 0)
+                    continue;
+                if (is_k) {  // the item's Q, once its predecessor's last Q.K^T has read the buffer
+                    if (nq > 0 && !mbar_wait(q_empty, (nq - 1) & 1, S_WAIT_LIMIT)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(q_full, STILE);
                     for (int dh = 0; dh < 2; ++dh)
-                        tma_load_3d(ring + s * STILE + dh * DBOX + hh * HBOX, map, full, dh * 64, int(j0[hh]), kvh);
-                ++issued;
+                        tma_load_3d(base + S_Q + dh * DBOX, &p.tq, q_full, dh * 64, int(t.row0), int(h));
+                }
+                ++nq;
+                uint32_t rawn[2] = {raw_entry(p, t, h, 0, 0), raw_entry(p, t, h, 0, 1)};
+                for (uint32_t pi = 0; pi < t.np; ++pi) {
+                    uint32_t j0[2], hi;
+                    keys_of(p, t, pi, 0, rawn[0], j0[0], hi);
+                    keys_of(p, t, pi, 1, rawn[1], j0[1], hi);
+                    if (pi + 1 < t.np) {  // the next pass's list entries are read while this pass waits for its stage
+                        rawn[0] = raw_entry(p, t, h, pi + 1, 0);
+                        rawn[1] = raw_entry(p, t, h, pi + 1, 1);
+                    }
+                    const uint32_t gi = g + pi, s = gi % nst, ph = (gi / nst) & 1;
+                    if (gi >= nst && !mbar_wait(is_k ? k_empty(s) : v_empty(s), ph ^ 1, S_WAIT_LIMIT)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full = is_k ? k_full(s) : v_full(s);
+                    mbar_expect_tx(full, STILE);
+                    for (uint32_t hh = 0; hh < 2; ++hh)
+                        for (int dh = 0; dh < 2; ++dh)
+                            tma_load_3d(ring + s * STILE + dh * DBOX + hh * HBOX, map, full, dh * 64, int(j0[hh]),
+                                        kvh);
+                    ++issued;
+                }
+                g += t.np;
             }
             if (!ok)
                 atomicExch(p.err, 11);
             // Our copies in flight land before the CTA leaves (already so on the normal path).
-            if (is_k)
-                mbar_wait(q_full, 0, S_WAIT_LIMIT);
-            for (uint32_t i = issued > nst ? issued - nst : 0; i < issued; ++i)
-                mbar_wait(is_k ? k_full(i % nst) : v_full(i % nst), (i / nst) & 1, S_WAIT_LIMIT);
-        }
-    } else if (warp == 1) {
-        // ---------------- UMMA issuer ----------------
-        // Fixed order QK(0), QK(1), then per pass PV(i), QK(i + 2): QK(i + 2) needs only the softmax to have read
-        // S(i), which it did before writing P(i), so both products of a pass go to the tensor core back to back.
-        // Each group is followed by one commit (s_full / pv_done); the K and V stages are released by a softmax
-        // thread that observes those completions anyway.
-        if (lane == 0 && t.np > 0) {
+            if (is_k && nq > 0)
+                mbar_wait(q_full, (nq - 1) & 1, S_WAIT_LIMIT);
+            for (uint32_t k = issued > nst ? issued - nst : 0; k < issued; ++k)
+                mbar_wait(is_k ? k_full(k % nst) : v_full(k % nst), (k / nst) & 1, S_WAIT_LIMIT);
+        } else if (warp == 1 && lane == 0) {
+            // ---------------- UMMA issuer ----------------
+            // Fixed order per item QK(0), QK(1), then per pass PV(i), QK(i + 2): QK(i + 2) needs only the softmax to
+            // have read S(i), which it did before writing P(i), so both products of a pass go to the tensor core back
+            // to back.  Each group is followed by one commit (s_full / pv_done); the K and V stages are released by a
+            // softmax thread that observes those completions anyway.
             const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, 128, 128);
             const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, 128, SD);
-            auto qk = [&](uint32_t j) {
-                const uint32_t s = j % NSK, b = j & 1;
-                bool w = mbar_wait(k_full(s), (j / NSK) & 1, S_WAIT_LIMIT);
-                if (w && j >= 2)
-                    w = mbar_wait(s_free(b), ((j - 2) >> 1) & 1, S_WAIT_LIMIT);
+            auto qk = [&](uint32_t gj) {
+                const uint32_t s = gj % NSK, b = gj & 1;
+                bool w = mbar_wait(k_full(s), (gj / NSK) & 1, S_WAIT_LIMIT);
+                if (w && gj >= 2)
+                    w = mbar_wait(s_free(b), ((gj - 2) >> 1) & 1, S_WAIT_LIMIT);
                 if (!w)
                     return false;
                 fence_after();
@@ -277,212 +315,252 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 umma_commit(s_full(b));
                 return true;
             };
-            bool ok = mbar_wait(q_full, 0, S_WAIT_LIMIT);
-            fence_after();
-            ok = ok && qk(0) && (t.np < 2 || qk(1));
-            for (uint32_t i = 0; ok && i < t.np; ++i) {
-                const uint32_t s = i % NSV;
-                ok = mbar_wait(p_full(i & 1), (i >> 1) & 1, S_WAIT_LIMIT) &&
-                     mbar_wait(v_full(s), (i / NSV) & 1, S_WAIT_LIMIT);
-                if (!ok)
+            bool ok = true;
+            uint32_t g = 0, nq = 0;
+            for (uint32_t round = 0; ok; ++round) {
+                const uint32_t i = sp_item(round);
+                if (i >= n_items)
                     break;
+                uint32_t h, kvh;
+                const TileInfo t = item(i, h, kvh);
+                if (t.np == 0)
+                    continue;
+                ok = mbar_wait(q_full, nq & 1, S_WAIT_LIMIT);
+                ++nq;
                 fence_after();
+                ok = ok && qk(g) && (t.np < 2 || qk(g + 1));
+                if (ok && t.np <= 2)
+                    umma_commit(q_empty);
+                for (uint32_t pi = 0; ok && pi < t.np; ++pi) {
+                    const uint32_t gi = g + pi, s = gi % NSV;
+                    ok = mbar_wait(p_full(gi & 1), (gi >> 1) & 1, S_WAIT_LIMIT) &&
+                         mbar_wait(v_full(s), (gi / NSV) & 1, S_WAIT_LIMIT);
+                    if (!ok)
+                        break;
+                    fence_after();
 #pragma unroll
-                for (uint32_t kk = 0; kk < 8; ++kk)
-                    umma_ts(tmem + COL_O, tmem + COL_P + 64 * (i & 1) + kk * 8,
-                            sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024), idesc_pv, i > 0 || kk > 0);
-                umma_commit(pv_done);
-                if (i + 2 < t.np)
-                    ok = qk(i + 2);
+                    for (uint32_t kk = 0; kk < 8; ++kk)
+                        umma_ts(tmem + COL_O, tmem + COL_P + 64 * (gi & 1) + kk * 8,
+                                sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024), idesc_pv, pi > 0 || kk > 0);
+                    umma_commit(pv_done);
+                    if (pi + 2 < t.np) {
+                        ok = qk(gi + 2);
+                        if (ok && pi + 3 == t.np)
+                            umma_commit(q_empty);
+                    }
+                    if (pi + 1 == t.np)
+                        umma_commit(o_done);
+                }
+                g += t.np;
             }
             if (!ok)
                 atomicExch(p.err, 12);
             umma_commit(mma_done);  // every MMA issued above has finished before TMEM is freed
             mbar_wait(mma_done, 0, S_WAIT_LIMIT);
         }
-    } else if (warp >= 4) {
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
         // ---------------- softmax and epilogue: tile row `row`, column half `c` ----------------
         const uint32_t c = (warp - 4) >> 2, qd = warp & 3, row = qd * 32 + lane, hr = row >> 6;
         const uint32_t tl = tmem + ((qd * 32) << 16);
         float* const xmax = reinterpret_cast<float*>(gbase + S_XMAX);
         float* const lsum = reinterpret_cast<float*>(gbase + S_LSUM);
+        uint32_t* const lcache = reinterpret_cast<uint32_t*>(gbase + S_LIST);
         const float scale = p.scale_log2;
         const uint64_t scale2 = pack2(scale, scale);
         bool ok = true;
-        // this row's cube list, copied to shared memory once (the loop reads it without global-load latency)
-        uint32_t* const lcache = reinterpret_cast<uint32_t*>(gbase + S_LIST);
-        const bool cached = t.cube && t.ncp <= kListCache;
-        if (cached)
-            for (uint32_t k = threadIdx.x - 128; k < 2 * kListCache; k += 256) {
-                const uint32_t hh = k / kListCache, pi = k % kListCache;
-                if (pi < t.ncp)
-                    lcache[k] = raw_entry(p, t, h, pi, hh);
-            }
-        named_bar(5, 256);
-        float m = -INFINITY, l = 0.0f;
+        uint32_t g = 0, nq = 0;
+        // Every softmax thread walks all of its CTA's items, also after a failed wait (then without waiting or
+        // computing), so that partners keep meeting at the named barriers, which cannot time out.  An item without
+        // passes (no key at all) stores zeros.
+        for (uint32_t round = 0;; ++round) {
+            const uint32_t ii = sp_item(round);
+            if (ii >= n_items)
+                break;
+            uint32_t h, kvh;
+            const TileInfo t = item(ii, h, kvh);
+            // this row's cube list, copied to shared memory once per item (the loop reads it without global-load
+            // latency); the barrier also keeps a fast thread from overwriting entries a slow one still reads
+            const bool cached = t.cube && t.ncp <= kListCache;
+            named_bar(5, 256);
+            if (cached)
+                for (uint32_t k = threadIdx.x - 128; k < 2 * kListCache; k += 256) {
+                    const uint32_t hh = k / kListCache, pi = k % kListCache;
+                    if (pi < t.ncp)
+                        lcache[k] = raw_entry(p, t, h, pi, hh);
+                }
+            named_bar(5, 256);
+            float m = -INFINITY, l = 0.0f;
 
-        // One pass over this thread's columns of S in NCH chunks of 32 (1: half of a cube pass's 64 keys; 2: half of
-        // 128 keys, the first chunk read again from TMEM for its exponentials so that only 32 scores are live).
-        // After a failed wait the thread skips the work but keeps meeting its partner at the named barrier (which
-        // cannot time out), so both column halves run the same number of passes.
-        auto pass = [&](auto nch_tag, uint32_t i, uint32_t key0, uint32_t hi) {
-            constexpr int NCH = decltype(nch_tag)::value;
-            const uint32_t b = i & 1, pb = COL_P + 64 * b;
-            // S columns of chunk k and the packed P columns (buffer b) it fills
-            auto s_col = [&](int k) { return NCH == 1 ? b * 128 + 64 * hr + 32 * c : b * 128 + 64 * c + 32 * k; };
-            auto p_col = [&](int k) { return NCH == 1 ? pb + 32 * hr + 16 * c : pb + 32 * c + 16 * k; };
-            uint32_t r[32];
-            float pmax = -INFINITY;
-            if (ok) {
-                fence_after();
+            // One pass over this thread's columns of S in NCH chunks of 32 (1: half of a cube pass's 64 keys; 2: half
+            // of 128 keys, the first chunk read again from TMEM for its exponentials so that only 32 scores are
+            // live).  After a failed wait the thread skips the work but keeps meeting its partner at the named
+            // barrier (which cannot time out), so both column halves run the same number of passes.
+            auto pass = [&](auto nch_tag, uint32_t pi, uint32_t key0, uint32_t hi) {
+                constexpr int NCH = decltype(nch_tag)::value;
+                const uint32_t gi = g + pi, b = gi & 1, pb = COL_P + 64 * b;
+                // S columns of chunk k and the packed P columns (buffer b) it fills
+                auto s_col = [&](int k) { return NCH == 1 ? b * 128 + 64 * hr + 32 * c : b * 128 + 64 * c + 32 * k; };
+                auto p_col = [&](int k) { return NCH == 1 ? pb + 32 * hr + 16 * c : pb + 32 * c + 16 * k; };
+                uint32_t r[32];
+                float pmax = -INFINITY;
+                if (ok) {
+                    fence_after();
 #pragma unroll
-                for (int k = 0; k < NCH; ++k) {
-                    tmem_ld32(tl + s_col(k), r);
-                    tmem_wait_ld();
-                    reg_fence(r);
-                    if (NCH == 1) {
-                        fence_before();
-                        mbar_arrive(s_free(b));  // Q K^T(i + 2) may overwrite this buffer now
+                    for (int k = 0; k < NCH; ++k) {
+                        tmem_ld32(tl + s_col(k), r);
+                        tmem_wait_ld();
+                        reg_fence(r);
+                        if (NCH == 1) {
+                            fence_before();
+                            mbar_arrive(s_free(b));  // Q K^T(i + 2) may overwrite this buffer now
+                        }
+                        mask_keys<32>(r, p.valid, key0 + 32 * k, hi);
+                        float mq[4] = {pmax, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                        for (int cc = 0; cc < 32; cc += 8)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                mq[e] = max3f(mq[e], __uint_as_float(r[cc + 2 * e]), __uint_as_float(r[cc + 2 * e + 1]));
+                        pmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
                     }
-                    mask_keys<32>(r, p.valid, key0 + 32 * k, hi);
-                    float mq[4] = {pmax, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-                    for (int cc = 0; cc < 32; cc += 8)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            mq[e] = max3f(mq[e], __uint_as_float(r[cc + 2 * e]), __uint_as_float(r[cc + 2 * e + 1]));
-                    pmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
                 }
-            }
-            // the row maximum over both column halves (partner: the same row in the other warpgroup)
-            xmax[(b * 2 + c) * 128 + row] = pmax;
-            named_bar(1 + qd, 64);
-            if (!ok)
-                return;
-            const float mx = fmaxf(pmax, xmax[(b * 2 + (c ^ 1)) * 128 + row]) * scale;
-            float f = 1.0f;
-            bool resc = false;
-            if (mx > m + 8.0f) {
-                f = m == -INFINITY ? 0.0f : ex2(m - mx);
-                m = mx;
-                l *= f;
-                resc = true;
-            }
-            const float mneg = m == -INFINITY ? 0.0f : -m;
-            const uint64_t mneg2 = pack2(mneg, mneg);
-            // P of the 32 scores in r as fp16 pairs, in place: pair cc into r[cc]
-            auto exps = [&]() {
-                uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
-#pragma unroll
-                for (int cc = 0; cc < 16; ++cc) {
-                    float a, bb;
-                    unpack2(ffma2(pack2(__uint_as_float(r[2 * cc]), __uint_as_float(r[2 * cc + 1])), scale2, mneg2), a,
-                            bb);
-                    a = ex2(a);
-                    bb = ex2(bb);
-                    sum2[cc & 1] = fadd2(sum2[cc & 1], pack2(a, bb));
-                    r[cc] = pack_half2s(a, bb);
-                }
-                float s0, s1, s2, s3;
-                unpack2(sum2[0], s0, s1);
-                unpack2(sum2[1], s2, s3);
-                l += (s0 + s1) + (s2 + s3);
-            };
-            exps();  // the chunk still in registers (the last one read)
-            // A rescale of O waits for P.V(i - 1), which adds to it (P.V(i) waits for this thread's P(i)); P(i)'s
-            // buffer was last read by P.V(i - 2), which finished before Q K^T(i) (committed after it).
-            if (i > 0 && __any_sync(0xffffffffu, resc)) {
-                ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, S_WAIT_LIMIT));
+                // the row maximum over both column halves (partner: the same row in the other warpgroup)
+                xmax[(b * 2 + c) * 128 + row] = pmax;
+                named_bar(1 + qd, 64);
                 if (!ok)
                     return;
-                fence_after();
-                {
-                    const float g = resc ? f : 1.0f;
+                const float mx = fmaxf(pmax, xmax[(b * 2 + (c ^ 1)) * 128 + row]) * scale;
+                float f = 1.0f;
+                bool resc = false;
+                if (mx > m + 8.0f) {
+                    f = m == -INFINITY ? 0.0f : ex2(m - mx);
+                    m = mx;
+                    l *= f;
+                    resc = true;
+                }
+                const float mneg = m == -INFINITY ? 0.0f : -m;
+                const uint64_t mneg2 = pack2(mneg, mneg);
+                // P of the 32 scores in r as fp16 pairs, in place: pair cc into r[cc]
+                auto exps = [&]() {
+                    uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
 #pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        uint32_t o[32];
-                        tmem_ld32(tl + COL_O + 64 * c + 32 * k, o);
-                        tmem_wait_ld();
-                        reg_fence(o);
+                    for (int cc = 0; cc < 16; ++cc) {
+                        float a, bb;
+                        unpack2(ffma2(pack2(__uint_as_float(r[2 * cc]), __uint_as_float(r[2 * cc + 1])), scale2, mneg2),
+                                a, bb);
+                        a = ex2(a);
+                        bb = ex2(bb);
+                        sum2[cc & 1] = fadd2(sum2[cc & 1], pack2(a, bb));
+                        r[cc] = pack_half2s(a, bb);
+                    }
+                    float s0, s1, s2, s3;
+                    unpack2(sum2[0], s0, s1);
+                    unpack2(sum2[1], s2, s3);
+                    l += (s0 + s1) + (s2 + s3);
+                };
+                exps();  // the chunk still in registers (the last one read)
+                // A rescale of O waits for P.V(i - 1), which adds to it (P.V(i) waits for this thread's P(i)); P(i)'s
+                // buffer was last read by P.V(i - 2), which finished before Q K^T(i) (committed after it).
+                if (pi > 0 && __any_sync(0xffffffffu, resc)) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (gi - 1) & 1, S_WAIT_LIMIT));
+                    if (!ok)
+                        return;
+                    fence_after();
+                    {
+                        const float gsc = resc ? f : 1.0f;
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            o[e] = __float_as_uint(__uint_as_float(o[e]) * g);
-                        tmem_st32(tl + COL_O + 64 * c + 32 * k, o);
+                        for (int k = 0; k < 2; ++k) {
+                            uint32_t o[32];
+                            tmem_ld32(tl + COL_O + 64 * c + 32 * k, o);
+                            tmem_wait_ld();
+                            reg_fence(o);
+#pragma unroll
+                            for (int e = 0; e < 32; ++e)
+                                o[e] = __float_as_uint(__uint_as_float(o[e]) * gsc);
+                            tmem_st32(tl + COL_O + 64 * c + 32 * k, o);
+                        }
                     }
                 }
-            }
-            tmem_st16(tl + p_col(NCH - 1), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-            if (NCH == 1) {
-                // the other cube's packed columns of this row are zeros
-                tmem_st16_zero(tl + pb + 32 * (hr ^ 1) + 16 * c);
-            } else {
-                tmem_ld32(tl + s_col(0), r);
-                tmem_wait_ld();
-                reg_fence(r);
+                tmem_st16(tl + p_col(NCH - 1), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+                if (NCH == 1) {
+                    // the other cube's packed columns of this row are zeros
+                    tmem_st16_zero(tl + pb + 32 * (hr ^ 1) + 16 * c);
+                } else {
+                    tmem_ld32(tl + s_col(0), r);
+                    tmem_wait_ld();
+                    reg_fence(r);
+                    fence_before();
+                    mbar_arrive(s_free(b));
+                    mask_keys<32>(r, p.valid, key0, hi);
+                    exps();
+                    tmem_st16(tl + p_col(0), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+                }
+                tmem_wait_st();
                 fence_before();
-                mbar_arrive(s_free(b));
-                mask_keys<32>(r, p.valid, key0, hi);
-                exps();
-                tmem_st16(tl + p_col(0), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-            }
-            tmem_wait_st();
-            fence_before();
-            mbar_arrive(p_full(b));
-        };
+                mbar_arrive(p_full(b));
+            };
 
-        for (uint32_t i = 0; i < t.np; ++i) {
-            const bool half = t.cube && i < t.ncp;  // this row sees only its cube's 64 keys
-            uint32_t j0, hi;
-            const uint32_t hh = half ? hr : 0;
-            keys_of(p, t, i, hh, half ? (cached ? lcache[hh * kListCache + i] : raw_entry(p, t, h, i, hh)) : 0u, j0,
-                    hi);
-            if (ok)
-                ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, S_WAIT_LIMIT));
-            if (ok && threadIdx.x == 128) {
-                mbar_arrive(k_empty(i % NSK));  // QK(i) has finished reading K(i)
-                if (i >= 2)
-                    mbar_arrive(v_empty((i - 2) % NSV));  // and PV(i - 2), committed before it, V(i - 2)
+            for (uint32_t pi = 0; pi < t.np; ++pi) {
+                const uint32_t gi = g + pi;
+                const bool half = t.cube && pi < t.ncp;  // this row sees only its cube's 64 keys
+                uint32_t j0, hi;
+                const uint32_t hh = half ? hr : 0;
+                keys_of(p, t, pi, hh,
+                        half ? (cached ? lcache[hh * kListCache + pi] : raw_entry(p, t, h, pi, hh)) : 0u, j0, hi);
+                if (ok)
+                    ok = __all_sync(0xffffffffu, mbar_wait(s_full(gi & 1), (gi >> 1) & 1, S_WAIT_LIMIT));
+                if (ok && threadIdx.x == 128) {
+                    mbar_arrive(k_empty(gi % NSK));  // QK(i) has finished reading K(i)
+                    if (gi >= 2)
+                        mbar_arrive(v_empty((gi - 2) % NSV));  // and PV(i - 2), committed before it, V(i - 2)
+                }
+                if (half)
+                    pass(std::integral_constant<int, 1>{}, pi, j0 + 32 * c, hi);
+                else
+                    pass(std::integral_constant<int, 2>{}, pi, j0 + 64 * c, hi);
             }
-            if (half)
-                pass(std::integral_constant<int, 1>{}, i, j0 + 32 * c, hi);
-            else
-                pass(std::integral_constant<int, 2>{}, i, j0 + 64 * c, hi);
-        }
-        if (ok && t.np > 0) {  // O is final once the issuer's last commit lands
-            ok = __all_sync(0xffffffffu, mbar_wait(mma_done, 0, S_WAIT_LIMIT));
-            fence_after();
+            if (ok && t.np > 0) {  // O is final once the item's last P.V lands
+                ok = __all_sync(0xffffffffu, mbar_wait(o_done, nq & 1, S_WAIT_LIMIT));
+                fence_after();
+            }
+            nq += t.np > 0;
+            g += t.np;
+            // the row sum over both halves
+            lsum[c * 128 + row] = l;
+            named_bar(1 + qd, 64);
+            l = lsum[row] + lsum[128 + row];
+            // Store: rows below n_q that belong to this tile (a cube tile's half past the last cube is another
+            // tile's).
+            const uint32_t grow = t.row0 + row;
+            bool store = t.active && grow < p.n_q && (!t.cube || t.cube_id[hr] < p.n_cubes);
+            int64_t dst = grow;
+            if (store && p.map) {
+                dst = p.map[grow];
+                store = dst >= 0;
+            }
+            const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
+            const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * c;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                uint32_t o[32];
+                if (ok && t.np > 0) {
+                    tmem_ld32(tl + COL_O + 64 * c + 32 * k, o);
+                    tmem_wait_ld();
+                    reg_fence(o);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        o[e] = 0u;
+                }
+                if (store)
+                    out_store32(p.o, orow + 32 * k, o, inv, p.o_type);
+            }
+            // the partner's sum is read before either thread's next item writes lsum again
+            named_bar(1 + qd, 64);
         }
         if (!ok && lane == 0)
             atomicExch(p.err, 13);
-        // the row sum over both halves
-        lsum[c * 128 + row] = l;
-        named_bar(1 + qd, 64);
-        l = lsum[row] + lsum[128 + row];
-        // Store: rows below n_q that belong to this tile (a cube tile's half past the last cube is another tile's).
-        const uint32_t grow = t.row0 + row;
-        bool store = t.active && grow < p.n_q && (!t.cube || t.cube_id[hr] < p.n_cubes);
-        int64_t dst = grow;
-        if (store && p.map) {
-            dst = p.map[grow];
-            store = dst >= 0;
-        }
-        const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
-        const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * c;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            uint32_t o[32];
-            if (ok && t.np > 0) {
-                tmem_ld32(tl + COL_O + 64 * c + 32 * k, o);
-                tmem_wait_ld();
-                reg_fence(o);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 32; ++e)
-                    o[e] = 0u;
-            }
-            if (store)
-                out_store32(p.o, orow + 32 * k, o, inv, p.o_type);
-        }
     }
     __syncwarp();
     fence_before();
@@ -537,7 +615,8 @@ cudaError_t launch_attn_tc_sparse(const AttnParams& a, int dtype, bool sel_i32, 
         return e;
     if (p.tiles_total == 0)
         return cudaSuccess;
-    attn_tc_sparse_kernel<<<dim3(p.tiles_total, a.heads), SNT, S_TOTAL, st>>>(p);
+    const uint32_t n_items = p.tiles_total * a.heads, sms = a.num_sms ? a.num_sms : 148;
+    attn_tc_sparse_kernel<<<n_items < sms ? n_items : sms, SNT, S_TOTAL, st>>>(p);
     return cudaGetLastError();
 }
 
