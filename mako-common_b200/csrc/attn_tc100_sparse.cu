@@ -38,12 +38,11 @@ constexpr uint32_t DBOX = 128 * 64 * 2;  // one d-half of a 128-row tile: 16 KB
 constexpr uint32_t HBOX = 64 * 64 * 2;   // a 64-row x 64-value TMA box: 8 KB
 constexpr uint32_t STILE = 2 * DBOX;     // 128 rows x 128 values
 constexpr uint32_t S_Q = 0, S_K = STILE, S_V = S_K + NSK * STILE, S_BAR = S_V + NSV * STILE;
-constexpr uint32_t S_XMAX = S_BAR + 256;   // float [2 passes][2 column halves][128 rows]: partial row maxima
-constexpr uint32_t S_LSUM = S_XMAX + 2048;  // float [2 column halves][128 rows]: partial row sums
+constexpr uint32_t S_STAT = S_BAR + 256;   // float2 [2 parities][128 rows]: each parity's (max, sum) per row
 constexpr uint32_t kListCache = 1024;        // list entries per cube kept in shared memory
-constexpr uint32_t S_LIST = S_LSUM + 1024;  // uint32 [2 cubes][kListCache]
+constexpr uint32_t S_LIST = S_STAT + 2048;  // uint32 [2 cubes][kListCache]
 constexpr uint32_t S_TOTAL = S_LIST + 2 * kListCache * 4 + 1024;
-constexpr uint32_t COL_O = 256, COL_P = 384;  // P: two buffers of 64 columns
+constexpr uint32_t COL_O = 256;  // O of parity x at COL_O + 128 x; S (and the P that replaces it) of parity x at 128 x
 constexpr long long S_WAIT_LIMIT = 1ll << 31;
 
 struct __align__(64) SpParams {
@@ -160,15 +159,22 @@ __device__ __forceinline__ void mask_keys(uint32_t (&r)[NC], const uint8_t* vali
 
 // Work item i of tiles_total * heads: head h = i / tiles_total, row tile u = tiles_total - 1 - i % tiles_total (the
 // tiles after the cubes, which see every key, first).  Consecutive items share a head, so the CTAs in flight read the
-// keys of a few heads and those stay in L2.  A persistent CTA takes one item per round of gridDim.x items, snaking as the
-// dense kernel does; while the softmax warps store one item's output, the producers load the next item's Q and first
-// key cubes and the issuer starts its Q.K^T.
+// keys of a few heads and those stay in L2.  A persistent CTA takes one item per round of gridDim.x items, snaking as
+// the dense kernel does; while the softmax warps store one item's output, the producers load the next item's Q and
+// first key cubes and the issuer starts its Q.K^T.
 __device__ __forceinline__ uint32_t sp_item(uint32_t round)
 {
     const uint32_t G = gridDim.x, c = (round & 1) ? G - 1 - blockIdx.x : blockIdx.x;
     return round * G + c;
 }
 
+// Passes alternate between two parities, each with its own S buffer and its own O accumulator and softmax
+// warpgroup: parity x takes the passes whose running number (over the CTA's items) has x as its low bit, and runs an
+// online softmax of its own over them (its own row maxima and sums).  The epilogue merges the two parities' (O, max,
+// sum) per row by log-sum-exp.  A pass's P replaces its S in place (P.V reads it from TMEM); Q.K^T of pass i + 2 into
+// the same buffer is issued right behind P.V(i): the tensor pipe executes one thread's MMAs in issue order.  So the
+// two parities' chains (softmax -> P.V -> Q.K^T -> softmax) interleave on the tensor core, and no row's softmax waits
+// for another thread.
 __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_constant__ SpParams p)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -180,13 +186,12 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     auto k_empty = [&](uint32_t s) { return sB + 24 + 8 * s; };
     auto v_full = [&](uint32_t s) { return sB + 48 + 8 * s; };
     auto v_empty = [&](uint32_t s) { return sB + 72 + 8 * s; };
-    auto s_full = [&](uint32_t b) { return sB + 96 + 8 * b; };
-    auto s_free = [&](uint32_t b) { return sB + 112 + 8 * b; };
-    auto p_full = [&](uint32_t b) { return sB + 128 + 8 * b; };
-    const uint32_t pv_done = sB + 144, q_full = sB + 152, mma_done = sB + 160;
+    auto s_full = [&](uint32_t x) { return sB + 96 + 8 * x; };
+    auto p_full = [&](uint32_t x) { return sB + 112 + 8 * x; };
+    auto o_done = [&](uint32_t x) { return sB + 128 + 8 * x; };  // the item's last P.V of parity x has finished
+    const uint32_t q_full = sB + 152, mma_done = sB + 160;
     const uint32_t tmem_slot = sB + 168;
     const uint32_t q_empty = sB + 176;  // an item's last Q.K^T has finished: Q may be overwritten
-    const uint32_t o_done = sB + 184;   // an item's last P.V has finished: O is final
     volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -204,16 +209,13 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             mbar_init(v_full(s), 1);
             mbar_init(v_empty(s), 1);
         }
-        for (uint32_t b = 0; b < 2; ++b) {
-            mbar_init(s_full(b), 1);
-            mbar_init(s_free(b), 256);
+        for (uint32_t x = 0; x < 2; ++x) {
+            mbar_init(s_full(x), 1);
+            mbar_init(p_full(x), 4);  // one arrival per warp of the parity's warpgroup
+            mbar_init(o_done(x), 1);
         }
-        mbar_init(p_full(0), 256);
-        mbar_init(p_full(1), 256);
-        mbar_init(pv_done, 1);
         mbar_init(q_full, 1);
         mbar_init(q_empty, 1);
-        mbar_init(o_done, 1);
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
@@ -226,8 +228,9 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     fence_after();
     const uint32_t tmem = *tmem_slot_ptr;
 
-    // Counters every role keeps alike: g counts the passes of the items so far (ring stages, S / P buffers and the
-    // phases of their barriers), nq the items with passes (Q loads, q_empty and o_done phases).
+    // Counters every role keeps alike: g counts the passes of the items so far (ring stages, parities and the phases
+    // of their barriers), nq the items with passes (Q loads and q_empty phases), nd[x] the items with a pass of
+    // parity x (o_done(x) phases).
     if (warp < 4) {
         // the producer / issuer warpgroup gives registers to the softmax warpgroups (384 x 168 at launch =
         // 128 x 104 + 256 x 200)
@@ -293,26 +296,21 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 mbar_wait(is_k ? k_full(k % nst) : v_full(k % nst), (k / nst) & 1, S_WAIT_LIMIT);
         } else if (warp == 1 && lane == 0) {
             // ---------------- UMMA issuer ----------------
-            // Fixed order per item QK(0), QK(1), then per pass PV(i), QK(i + 2): QK(i + 2) needs only the softmax to
-            // have read S(i), which it did before writing P(i), so both products of a pass go to the tensor core back
-            // to back.  Each group is followed by one commit (s_full / pv_done); the K and V stages are released by a
-            // softmax thread that observes those completions anyway.
+            // Per item QK(0), QK(1), then per pass PV(i), QK(i + 2), both into parity i's buffers, one commit per
+            // Q.K^T; the K and V stages are released by a softmax thread that observes those completions anyway.
             const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, 128, 128);
             const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, 128, SD);
             auto qk = [&](uint32_t gj) {
-                const uint32_t s = gj % NSK, b = gj & 1;
-                bool w = mbar_wait(k_full(s), (gj / NSK) & 1, S_WAIT_LIMIT);
-                if (w && gj >= 2)
-                    w = mbar_wait(s_free(b), ((gj - 2) >> 1) & 1, S_WAIT_LIMIT);
-                if (!w)
+                const uint32_t s = gj % NSK, x = gj & 1;
+                if (!mbar_wait(k_full(s), (gj / NSK) & 1, S_WAIT_LIMIT))
                     return false;
                 fence_after();
 #pragma unroll
                 for (uint32_t ks = 0; ks < SD / 16; ++ks)
-                    umma_ss(tmem + b * 128, sdesc(base + S_Q + (ks >> 2) * DBOX + (ks & 3) * 32, 16, 1024),
+                    umma_ss(tmem + x * 128, sdesc(base + S_Q + (ks >> 2) * DBOX + (ks & 3) * 32, 16, 1024),
                             sdesc(base + S_K + s * STILE + (ks >> 2) * DBOX + (ks & 3) * 32, 16, 1024), idesc_qk,
                             ks > 0);
-                umma_commit(s_full(b));
+                umma_commit(s_full(x));
                 return true;
             };
             bool ok = true;
@@ -332,24 +330,23 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 if (ok && t.np <= 2)
                     umma_commit(q_empty);
                 for (uint32_t pi = 0; ok && pi < t.np; ++pi) {
-                    const uint32_t gi = g + pi, s = gi % NSV;
-                    ok = mbar_wait(p_full(gi & 1), (gi >> 1) & 1, S_WAIT_LIMIT) &&
+                    const uint32_t gi = g + pi, x = gi & 1, s = gi % NSV;
+                    ok = mbar_wait(p_full(x), (gi >> 1) & 1, S_WAIT_LIMIT) &&
                          mbar_wait(v_full(s), (gi / NSV) & 1, S_WAIT_LIMIT);
                     if (!ok)
                         break;
                     fence_after();
 #pragma unroll
                     for (uint32_t kk = 0; kk < 8; ++kk)
-                        umma_ts(tmem + COL_O, tmem + COL_P + 64 * (gi & 1) + kk * 8,
-                                sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024), idesc_pv, pi > 0 || kk > 0);
-                    umma_commit(pv_done);
+                        umma_ts(tmem + COL_O + 128 * x, tmem + 128 * x + kk * 8,
+                                sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024), idesc_pv, pi >= 2 || kk > 0);
                     if (pi + 2 < t.np) {
                         ok = qk(gi + 2);
                         if (ok && pi + 3 == t.np)
                             umma_commit(q_empty);
+                    } else {
+                        umma_commit(o_done(x));  // parity x's last product of the item
                     }
-                    if (pi + 1 == t.np)
-                        umma_commit(o_done);
                 }
                 g += t.np;
             }
@@ -360,27 +357,27 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         }
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
-        // ---------------- softmax and epilogue: tile row `row`, column half `c` ----------------
-        const uint32_t c = (warp - 4) >> 2, qd = warp & 3, row = qd * 32 + lane, hr = row >> 6;
+        // ---------------- softmax of parity x and the epilogue: tile row `row` ----------------
+        const uint32_t x = (warp - 4) >> 2, qd = warp & 3, row = qd * 32 + lane, hr = row >> 6;
         const uint32_t tl = tmem + ((qd * 32) << 16);
-        float* const xmax = reinterpret_cast<float*>(gbase + S_XMAX);
-        float* const lsum = reinterpret_cast<float*>(gbase + S_LSUM);
+        const uint32_t colS = 128 * x, colO = COL_O + 128 * x;
+        float2* const stat = reinterpret_cast<float2*>(gbase + S_STAT);
         uint32_t* const lcache = reinterpret_cast<uint32_t*>(gbase + S_LIST);
         const float scale = p.scale_log2;
         const uint64_t scale2 = pack2(scale, scale);
         bool ok = true;
-        uint32_t g = 0, nq = 0;
+        uint32_t g = 0, nd = 0;  // nd: items with a pass of this parity
         // Every softmax thread walks all of its CTA's items, also after a failed wait (then without waiting or
-        // computing), so that partners keep meeting at the named barriers, which cannot time out.  An item without
-        // passes (no key at all) stores zeros.
+        // computing), so that the two parities keep meeting at the named barriers, which cannot time out.  An item
+        // without passes (no key at all) stores zeros.
         for (uint32_t round = 0;; ++round) {
             const uint32_t ii = sp_item(round);
             if (ii >= n_items)
                 break;
             uint32_t h, kvh;
             const TileInfo t = item(ii, h, kvh);
-            // this row's cube list, copied to shared memory once per item (the loop reads it without global-load
-            // latency); the barrier also keeps a fast thread from overwriting entries a slow one still reads
+            // this item's cube lists, copied to shared memory once (the passes read them without global-load
+            // latency); the first barrier also keeps a fast thread from overwriting entries a slow one still reads
             const bool cached = t.cube && t.ncp <= kListCache;
             named_bar(5, 256);
             if (cached)
@@ -391,46 +388,30 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 }
             named_bar(5, 256);
             float m = -INFINITY, l = 0.0f;
+            uint32_t mine = 0;  // passes of this parity in the item
 
-            // One pass over this thread's columns of S in NCH chunks of 32 (1: half of a cube pass's 64 keys; 2: half
-            // of 128 keys, the first chunk read again from TMEM for its exponentials so that only 32 scores are
-            // live).  After a failed wait the thread skips the work but keeps meeting its partner at the named
-            // barrier (which cannot time out), so both column halves run the same number of passes.
-            auto pass = [&](auto nch_tag, uint32_t pi, uint32_t key0, uint32_t hi) {
-                constexpr int NCH = decltype(nch_tag)::value;
-                const uint32_t gi = g + pi, b = gi & 1, pb = COL_P + 64 * b;
-                // S columns of chunk k and the packed P columns (buffer b) it fills
-                auto s_col = [&](int k) { return NCH == 1 ? b * 128 + 64 * hr + 32 * c : b * 128 + 64 * c + 32 * k; };
-                auto p_col = [&](int k) { return NCH == 1 ? pb + 32 * hr + 16 * c : pb + 32 * c + 16 * k; };
-                uint32_t r[32];
-                float pmax = -INFINITY;
-                if (ok) {
-                    fence_after();
+            // One pass of this parity: S (NK columns of this row from column c0) to P in place.  NK 64: a cube pass,
+            // the row's own cube half (the other half's P is zero); NK 128: every column.
+            auto pass = [&](auto nk_tag, uint32_t c0, uint32_t key0, uint32_t hi) {
+                constexpr int NK = decltype(nk_tag)::value;
+                uint32_t r[NK / 32][32];
 #pragma unroll
-                    for (int k = 0; k < NCH; ++k) {
-                        tmem_ld32(tl + s_col(k), r);
-                        tmem_wait_ld();
-                        reg_fence(r);
-                        if (NCH == 1) {
-                            fence_before();
-                            mbar_arrive(s_free(b));  // Q K^T(i + 2) may overwrite this buffer now
-                        }
-                        mask_keys<32>(r, p.valid, key0 + 32 * k, hi);
-                        float mq[4] = {pmax, -INFINITY, -INFINITY, -INFINITY};
+                for (int k = 0; k < NK / 32; ++k)
+                    tmem_ld32(tl + colS + c0 + 32 * k, r[k]);
+                tmem_wait_ld();
 #pragma unroll
-                        for (int cc = 0; cc < 32; cc += 8)
-#pragma unroll
-                            for (int e = 0; e < 4; ++e)
-                                mq[e] = max3f(mq[e], __uint_as_float(r[cc + 2 * e]), __uint_as_float(r[cc + 2 * e + 1]));
-                        pmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-                    }
+                for (int k = 0; k < NK / 32; ++k) {
+                    reg_fence(r[k]);
+                    mask_keys<32>(r[k], p.valid, key0 + 32 * k, hi);
                 }
-                // the row maximum over both column halves (partner: the same row in the other warpgroup)
-                xmax[(b * 2 + c) * 128 + row] = pmax;
-                named_bar(1 + qd, 64);
-                if (!ok)
-                    return;
-                const float mx = fmaxf(pmax, xmax[(b * 2 + (c ^ 1)) * 128 + row]) * scale;
+                float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int c = 0; c < NK; c += 8)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        mq[e] = max3f(mq[e], __uint_as_float(r[(c + 2 * e) >> 5][(c + 2 * e) & 31]),
+                                      __uint_as_float(r[(c + 2 * e + 1) >> 5][(c + 2 * e + 1) & 31]));
+                const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
                 float f = 1.0f;
                 bool resc = false;
                 if (mx > m + 8.0f) {
@@ -441,97 +422,101 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 }
                 const float mneg = m == -INFINITY ? 0.0f : -m;
                 const uint64_t mneg2 = pack2(mneg, mneg);
-                // P of the 32 scores in r as fp16 pairs, in place: pair cc into r[cc]
-                auto exps = [&]() {
-                    uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
+                uint32_t pk[NK / 64][32];
+                uint64_t sum2[2] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f)};
 #pragma unroll
-                    for (int cc = 0; cc < 16; ++cc) {
-                        float a, bb;
-                        unpack2(ffma2(pack2(__uint_as_float(r[2 * cc]), __uint_as_float(r[2 * cc + 1])), scale2, mneg2),
-                                a, bb);
-                        a = ex2(a);
-                        bb = ex2(bb);
-                        sum2[cc & 1] = fadd2(sum2[cc & 1], pack2(a, bb));
-                        r[cc] = pack_half2s(a, bb);
-                    }
+                for (int c = 0; c < NK / 2; ++c) {
+                    float a, b;
+                    unpack2(ffma2(pack2(__uint_as_float(r[(2 * c) >> 5][(2 * c) & 31]),
+                                        __uint_as_float(r[(2 * c + 1) >> 5][(2 * c + 1) & 31])),
+                                  scale2, mneg2),
+                            a, b);
+                    a = ex2(a);
+                    b = ex2(b);
+                    sum2[c & 1] = fadd2(sum2[c & 1], pack2(a, b));
+                    pk[c >> 5][c & 31] = pack_half2s(a, b);
+                }
+                {
                     float s0, s1, s2, s3;
                     unpack2(sum2[0], s0, s1);
                     unpack2(sum2[1], s2, s3);
                     l += (s0 + s1) + (s2 + s3);
-                };
-                exps();  // the chunk still in registers (the last one read)
-                // A rescale of O waits for P.V(i - 1), which adds to it (P.V(i) waits for this thread's P(i)); P(i)'s
-                // buffer was last read by P.V(i - 2), which finished before Q K^T(i) (committed after it).
-                if (pi > 0 && __any_sync(0xffffffffu, resc)) {
-                    ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (gi - 1) & 1, S_WAIT_LIMIT));
-                    if (!ok)
-                        return;
-                    fence_after();
-                    {
-                        const float gsc = resc ? f : 1.0f;
-#pragma unroll
-                        for (int k = 0; k < 2; ++k) {
-                            uint32_t o[32];
-                            tmem_ld32(tl + COL_O + 64 * c + 32 * k, o);
-                            tmem_wait_ld();
-                            reg_fence(o);
-#pragma unroll
-                            for (int e = 0; e < 32; ++e)
-                                o[e] = __float_as_uint(__uint_as_float(o[e]) * gsc);
-                            tmem_st32(tl + COL_O + 64 * c + 32 * k, o);
-                        }
-                    }
                 }
-                tmem_st16(tl + p_col(NCH - 1), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-                if (NCH == 1) {
-                    // the other cube's packed columns of this row are zeros
-                    tmem_st16_zero(tl + pb + 32 * (hr ^ 1) + 16 * c);
+                // P over S's first 64 columns (two keys a column): a cube pass fills its cube's 32 and zeros the
+                // other 32; every S value this thread needs is in registers by now
+                if (NK == 64) {
+                    tmem_st32(tl + colS + 32 * hr, pk[0]);
+                    tmem_st16_zero(tl + colS + 32 * (hr ^ 1));
+                    tmem_st16_zero(tl + colS + 32 * (hr ^ 1) + 16);
                 } else {
-                    tmem_ld32(tl + s_col(0), r);
-                    tmem_wait_ld();
-                    reg_fence(r);
-                    fence_before();
-                    mbar_arrive(s_free(b));
-                    mask_keys<32>(r, p.valid, key0, hi);
-                    exps();
-                    tmem_st16(tl + p_col(0), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+#pragma unroll
+                    for (int k = 0; k < NK / 64; ++k)
+                        tmem_st32(tl + colS + 32 * k, pk[k]);
+                }
+                // Rescale this parity's O before P.V adds to it: its previous product, P.V(i - 2), finished before
+                // S(i) was seen (the commit that signalled S(i) tracks it).
+                if (__any_sync(0xffffffffu, resc && mine > 0)) {
+                    const float gsc = resc ? f : 1.0f;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        uint32_t o[32];
+                        tmem_ld32(tl + colO + 32 * k, o);
+                        tmem_wait_ld();
+                        reg_fence(o);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * gsc);
+                        tmem_st32(tl + colO + 32 * k, o);
+                    }
                 }
                 tmem_wait_st();
                 fence_before();
-                mbar_arrive(p_full(b));
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive_n(p_full(x), 1);
             };
 
             for (uint32_t pi = 0; pi < t.np; ++pi) {
                 const uint32_t gi = g + pi;
+                if ((gi & 1) != x)
+                    continue;
                 const bool half = t.cube && pi < t.ncp;  // this row sees only its cube's 64 keys
                 uint32_t j0, hi;
                 const uint32_t hh = half ? hr : 0;
                 keys_of(p, t, pi, hh,
                         half ? (cached ? lcache[hh * kListCache + pi] : raw_entry(p, t, h, pi, hh)) : 0u, j0, hi);
                 if (ok)
-                    ok = __all_sync(0xffffffffu, mbar_wait(s_full(gi & 1), (gi >> 1) & 1, S_WAIT_LIMIT));
-                if (ok && threadIdx.x == 128) {
-                    mbar_arrive(k_empty(gi % NSK));  // QK(i) has finished reading K(i)
+                    ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), (gi >> 1) & 1, S_WAIT_LIMIT));
+                if (ok && (threadIdx.x & 127) == 0) {
+                    // S(i) seen: Q.K^T(i) has finished reading K(i), and P.V(i - 2), committed before it, V(i - 2)
+                    mbar_arrive(k_empty(gi % NSK));
                     if (gi >= 2)
-                        mbar_arrive(v_empty((gi - 2) % NSV));  // and PV(i - 2), committed before it, V(i - 2)
+                        mbar_arrive(v_empty((gi - 2) % NSV));
                 }
-                if (half)
-                    pass(std::integral_constant<int, 1>{}, pi, j0 + 32 * c, hi);
-                else
-                    pass(std::integral_constant<int, 2>{}, pi, j0 + 64 * c, hi);
+                if (ok) {
+                    fence_after();
+                    if (half)
+                        pass(std::integral_constant<int, 64>{}, 64 * hr, j0, hi);
+                    else
+                        pass(std::integral_constant<int, 128>{}, 0, j0, hi);
+                }
+                ++mine;
             }
-            if (ok && t.np > 0) {  // O is final once the item's last P.V lands
-                ok = __all_sync(0xffffffffu, mbar_wait(o_done, nq & 1, S_WAIT_LIMIT));
+            if (ok && mine > 0) {  // this parity's O is final once its last P.V of the item lands
+                ok = __all_sync(0xffffffffu, mbar_wait(o_done(x), nd & 1, S_WAIT_LIMIT));
                 fence_after();
             }
-            nq += t.np > 0;
+            nd += mine > 0;
             g += t.np;
-            // the row sum over both halves
-            lsum[c * 128 + row] = l;
+            // Merge the parities: exchange (max, sum) with the other parity's thread of this row, then this thread
+            // stores output columns [64 x, 64 x + 64) from both parities' O.
+            stat[x * 128 + row] = make_float2(mine > 0 ? m : -INFINITY, mine > 0 ? l : 0.0f);
             named_bar(1 + qd, 64);
-            l = lsum[row] + lsum[128 + row];
-            // Store: rows below n_q that belong to this tile (a cube tile's half past the last cube is another
-            // tile's).
+            const float2 s0 = stat[row], s1 = stat[128 + row];
+            const float M = fmaxf(s0.x, s1.x);
+            const float w0 = s0.x == -INFINITY ? 0.0f : ex2(s0.x - M), w1 = s1.x == -INFINITY ? 0.0f : ex2(s1.x - M);
+            const float L = s0.y * w0 + s1.y * w1;
+            const bool has0 = ok && s0.x != -INFINITY, has1 = ok && s1.x != -INFINITY;
             const uint32_t grow = t.row0 + row;
             bool store = t.active && grow < p.n_q && (!t.cube || t.cube_id[hr] < p.n_cubes);
             int64_t dst = grow;
@@ -539,25 +524,29 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 dst = p.map[grow];
                 store = dst >= 0;
             }
-            const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
-            const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * c;
+            const float inv = (L > 0.0f ? 1.0f / L : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
+            const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * x;
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
-                uint32_t o[32];
-                if (ok && t.np > 0) {
-                    tmem_ld32(tl + COL_O + 64 * c + 32 * k, o);
-                    tmem_wait_ld();
-                    reg_fence(o);
-                } else {
+                // both parities' columns (warp-collective loads; a parity without passes in this item holds an older
+                // item's values, which the selects below leave out)
+                uint32_t o[32], o1[32];
+                tmem_ld32(tl + COL_O + 64 * x + 32 * k, o);
+                tmem_ld32(tl + COL_O + 128 + 64 * x + 32 * k, o1);
+                tmem_wait_ld();
+                reg_fence(o);
+                reg_fence(o1);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        o[e] = 0u;
-                }
+                for (int e = 0; e < 32; ++e)
+                    o[e] = __float_as_uint((has0 ? __uint_as_float(o[e]) * w0 : 0.0f) +
+                                           (has1 ? __uint_as_float(o1[e]) * w1 : 0.0f));
                 if (store)
                     out_store32(p.o, orow + 32 * k, o, inv, p.o_type);
             }
-            // the partner's sum is read before either thread's next item writes lsum again
+            // both parities' O (and the stat entries) are read before either parity's next item writes them
+            fence_before();
             named_bar(1 + qd, 64);
+            fence_after();
         }
         if (!ok && lane == 0)
             atomicExch(p.err, 13);
