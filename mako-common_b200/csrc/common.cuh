@@ -41,10 +41,31 @@ __device__ __forceinline__ void out_store2(void* o, uint64_t i, float a, float b
         *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(o) + i) = out_pack2(a, b, o_type);
 }
 // o[i .. i + 32) = r[0 .. 32) (fp32 bits) * s, i a multiple of 8 and o 16-byte aligned: 128-bit stores
+__device__ __forceinline__ void st_global_v8(void* d, const uint32_t (&w)[8])
+{
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"l"(d), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                 "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+}
+
+// 32 consecutive output values of one row (r[k] * s), fp32 or 16-bit.  32-byte stores (whole sectors) where the row
+// slice is 32-byte aligned, else 16-byte stores: a warp's 32 rows are 32 scattered slices, so fewer, fuller stores
+// cost less.
 __device__ __forceinline__ void out_store32(void* o, uint64_t i, const uint32_t (&r)[32], float s, uint32_t o_type)
 {
     if (o_type == 0) {
         float* d = static_cast<float*>(o) + i;
+        if ((reinterpret_cast<uintptr_t>(d) & 31) == 0) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                uint32_t w[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    w[k] = __float_as_uint(__uint_as_float(r[8 * e + k]) * s);
+                st_global_v8(d + 8 * e, w);
+            }
+            return;
+        }
 #pragma unroll
         for (int e = 0; e < 8; ++e)
             *reinterpret_cast<float4*>(d + 4 * e) =
@@ -53,6 +74,18 @@ __device__ __forceinline__ void out_store32(void* o, uint64_t i, const uint32_t 
         return;
     }
     uint16_t* d = static_cast<uint16_t*>(o) + i;
+    if ((reinterpret_cast<uintptr_t>(d) & 31) == 0) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            uint32_t w[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                w[k] = out_pack2(__uint_as_float(r[16 * e + 2 * k]) * s, __uint_as_float(r[16 * e + 2 * k + 1]) * s,
+                                 o_type);
+            st_global_v8(d + 16 * e, w);
+        }
+        return;
+    }
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         uint32_t w[4];

@@ -90,7 +90,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                  "r"(src), "r"(c0), "r"(c1)
                  : "memory");
 }
+// `bytes` (a multiple of 16) from this CTA's shared memory to global memory, both addresses 16-byte aligned, in the
+// current bulk group (untiled bulk copy: the copy engine does the global writes asynchronously).
+__device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(gdst), "r"(ssrc), "r"(bytes)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// Waits until every committed bulk copy of this thread has completed (its global writes included).
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 // Waits until every committed bulk store has finished reading shared memory (the writes may still be in flight).
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
