@@ -16,7 +16,7 @@
 namespace mako {
 namespace {
 
-constexpr int HW = 8;  // warps (rows) a CTA
+constexpr int HW = 4;  // warps (rows) a CTA
 
 template <typename T>
 __device__ __forceinline__ T to16(float v);
@@ -65,13 +65,31 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[VPL])
     }
 }
 
+// The (cos, sin) angle of each of this lane's values (value i < rot pairs with i +- rot / 2 and takes angle
+// i mod rot / 2; adjacent pairs 2i, 2i + 1 take angle i), loaded with the row's values so that both round trips to
+// memory overlap; (1, 0) past rot.
+template <int VPL>
+__device__ __forceinline__ void load_angles(const HeadsParams& p, const float2* cs, int lane, float2 (&ang)[VPL])
+{
+    const uint32_t half = p.rot / 2;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+        const uint32_t i = lane * VPL + k;
+        ang[k] = make_float2(1.0f, 0.0f);
+        if (p.rope == 2)
+            ang[k] = __ldg(cs + i / 2);
+        else if (i < p.rot)
+            ang[k] = __ldg(cs + (i < half ? i : i - half));
+    }
+}
+
 // The rest of row r (model row t) once the values of its nh heads from h0 are in registers: RMS norm, rotation and
-// the 16-bit stores (zeros for t < 0).  cs: the row's angles, wv: the norm weights of this
-// lane's values, buf: dim floats of per-warp scratch, used when rotation partners cross lanes unevenly.
+// the 16-bit stores (zeros for t < 0).  ang: the angles of this lane's values (load_angles), wv: their norm
+// weights, buf: dim floats of per-warp scratch, used when rotation partners cross lanes unevenly.
 template <int VPL, int NH, typename T>
 __device__ __forceinline__ void row_out(const HeadsParams& p, int32_t t, uint32_t r, uint32_t h0, uint32_t nh,
-                                        float (&v)[NH][VPL], const float (&wv)[VPL], const float2* cs, float* buf,
-                                        int lane)
+                                        float (&v)[NH][VPL], const float (&wv)[VPL], const float2 (&ang)[VPL],
+                                        float* buf, int lane)
 {
     T* const y0 = static_cast<T*>(p.y) + (uint64_t(h0) * p.n_pad + p.row0 + r) * p.dim + lane * VPL;
     const uint64_t ystep = uint64_t(p.n_pad) * p.dim;
@@ -84,22 +102,16 @@ __device__ __forceinline__ void row_out(const HeadsParams& p, int32_t t, uint32_
             store16<VPL, T>(y0 + j * ystep, z);
         return;
     }
-    // the angles of this lane's values (value i < rot pairs with i +- rot / 2, or 2i with 2i + 1)
+    // the sign of the partner's term: -s for the first of a pair, +s for the second
     float cc[VPL], sn[VPL];
     const uint32_t half = p.rot / 2;
     if (p.rope) {
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
             const uint32_t i = lane * VPL + k;
-            float2 c = make_float2(1.0f, 0.0f);
-            if (p.rope == 2)
-                c = cs[i / 2];
-            else if (i < p.rot)
-                c = cs[i < half ? i : i - half];
-            // the sign of the partner's term: -s for the first of a pair, +s for the second
             const bool first = p.rope == 2 ? (i & 1) == 0 : i < half;
-            cc[k] = c.x;
-            sn[k] = first ? -c.y : c.y;
+            cc[k] = ang[k].x;
+            sn[k] = first ? -ang[k].y : ang[k].y;
         }
     }
     // Every step runs over all NH heads at once (heads past nh hold zeros and are not stored), so the heads' shuffle
@@ -185,7 +197,7 @@ __device__ __forceinline__ void row_out(const HeadsParams& p, int32_t t, uint32_
 }
 
 template <int VPL, typename T>
-__global__ void __launch_bounds__(HW * 32, VPL <= 4 ? 4 : 2) heads_kernel(const HeadsParams p)
+__global__ void __launch_bounds__(HW * 32, VPL <= 4 ? 8 : 4) heads_kernel(const HeadsParams p)
 {
     __shared__ float row_buf[HW][VPL * 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -196,6 +208,7 @@ __global__ void __launch_bounds__(HW * 32, VPL <= 4 ? 4 : 2) heads_kernel(const 
     const int32_t t = p.map ? p.map[r] : int32_t(r);
     float v[HPW][VPL];
     float wv[VPL];
+    float2 ang[VPL];
     if (t >= 0) {
         // all the warp's heads of this row in flight at once
         const float* const x0 = p.x + uint64_t(t) * p.ld + p.col0 + uint64_t(h0) * p.stride + lane * VPL;
@@ -222,9 +235,10 @@ __global__ void __launch_bounds__(HW * 32, VPL <= 4 ? 4 : 2) heads_kernel(const 
 #pragma unroll
             for (int k = 0; k < VPL; ++k)
                 wv[k] = __ldg(p.w + lane * VPL + k);
+        if (p.rope)
+            load_angles<VPL>(p, reinterpret_cast<const float2*>(p.cs) + uint64_t(t) * p.cs_row, lane, ang);
     }
-    const float2* const cs = p.rope && t >= 0 ? reinterpret_cast<const float2*>(p.cs) + uint64_t(t) * p.cs_row : nullptr;
-    row_out<VPL, HPW, T>(p, t, r, h0, nh, v, wv, cs, row_buf[warp], lane);
+    row_out<VPL, HPW, T>(p, t, r, h0, nh, v, wv, ang, row_buf[warp], lane);
 }
 
 template <typename T>
