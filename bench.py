@@ -14,6 +14,8 @@ Workloads (synthetic seeded data -- no dataset is involve
   heads          the head-tile producers (RMS norm + RoPE into bf16 tiles) at configs[2]'s shape
   prefill_d256   not a BASELINE config: causal GQA prefill bf16 with Qwen3.5's 256-wide gated-attention heads,
                  16 / 2 heads, S 8192
+  proj           the output projection after configs[2]'s attention: 16384 x 4096 bf16 o times a 4096 x 4096 bf16
+                 matrix (the consumer of the attention's 16-bit output)
 A step is one call of the public C ABI (include/mako_attn.h) over one batch held in HBM; `value` is device time
 (CUDA events on the launching stream, max over ranks; L2 flushed between steps by a 256 MB write, except for an
 HBM-bound step whose inputs exceed 4x the 126 MB L2, `config.l2` says which); `e2e` is the same metric with the
@@ -408,6 +410,63 @@ class DecodeLong(Workload):
         return self.o.cpu().numpy(), want, "all 32 heads" + (" (rank 0's merged o)" if self.world > 1 else "")
 
 
+class Proj(Workload):
+    """The output projection after configs[2]'s attention: the 16-bit o of batch 2 x 8192 tokens x 32 heads of 128
+    (x [16384][4096] bf16) times the 4096 x 4096 bf16 matrix, fp32 y (mako_proj; Runtime::proj as
+    src/models/qwen_text.cpp:312 calls it).  Tensor-bound: 2 T k n FLOP."""
+    name, metric, unit, bound, dtype = "proj", "output projection TFLOP/s (bf16 GEMM after the attention)", \
+        "TFLOP/s", "tensor", "bf16"
+
+    def __init__(self, seed=0):
+        import torch
+        self.T, self.k, self.n = 2 * 8192, 32 * 128, 32 * 128
+        self.x = gen((self.T, self.k), torch.bfloat16, seed + 1, 0.5)
+        self.w = gen((self.n, self.k), torch.bfloat16, seed + 2, 0.02)
+        self.y = torch.empty((self.T, self.n), dtype=torch.float32, device=DEVICE)
+        self.inputs, self.outputs = [self.x, self.w], [self.y]
+        self.config = {"workload": "proj (configs[2]'s output projection: 16384 tokens x 4096 -> 4096, bf16)",
+                       "T": self.T, "k": self.k, "n": self.n, "dtype": "bf16", "seed": seed,
+                       "l2": "flushed between steps (256 MB write)"}
+
+    def work(self):
+        return 2.0 * self.T * self.k * self.n
+
+    def step(self, ctx):
+        ctx.proj(self.w, self.x, self.y, self.T, self.k, self.n)
+
+    def _bits(self):
+        import numpy as np
+        f = lambda t: t.cpu().view(torch_int16()).numpy().view(np.uint16)  # noqa: E731
+        return f(self.x), f(self.w)
+
+    def cpu_sample(self, O, threads, target_s=10.0):
+        import numpy as np
+        x, w = self._bits()
+        t0 = time.perf_counter()
+        O.proj(1, w, x, self.T, self.k, self.n, rows=np.arange(4, dtype=np.uint32), nthreads=threads)
+        dt = max(time.perf_counter() - t0, 1e-3)
+        rows = np.unique(np.linspace(0, self.T - 1, int(min(self.T, max(4, 4 * target_s / dt)))).astype(np.uint32))
+
+        def run():
+            return O.proj(1, w, x, self.T, self.k, self.n, rows=rows, nthreads=threads)
+        return run, 2.0 * len(rows) * self.k * self.n, f"{len(rows)} of {self.T} rows (evenly spaced), all " \
+                                                        f"{self.n} columns; rate extrapolated linearly in rows"
+
+    def check(self, O):
+        import numpy as np
+        x, w = self._bits()
+        rows = np.linspace(0, self.T - 1, 24).astype(np.uint32)
+        want = O.proj(1, w, x, self.T, self.k, self.n, rows=rows)
+        return self.y.cpu().numpy()[rows], want[rows], f"{len(rows)} rows x all columns"
+
+    tolerance = "relative L2 <= 1e-5 against the double-precision GEMM of the same bf16 inputs"
+
+    def within(self, got, want):
+        import numpy as np
+        err = np.asarray(got, np.float64) - np.asarray(want, np.float64)
+        return float(np.sqrt(np.sum(err ** 2) / max(np.sum(np.asarray(want, np.float64) ** 2), 1e-30))) <= 1e-5
+
+
 class Sparse(Workload):
     name, metric, unit, bound, dtype = "sparse", "block-sparse attention TFLOP/s on kept blocks", "TFLOP/s", \
         "tensor", "bf16"
@@ -577,6 +636,8 @@ def make_workload(name, world=1, rank=0):
         return Sparse()
     if name == "heads":
         return Heads()
+    if name == "proj":
+        return Proj()
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -910,7 +971,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="bidir",
                     choices=["decode", "decode_long", "prefill", "sparse", "bidir", "prefill_small", "prefill_d256",
-                             "heads"])
+                             "heads", "proj"])
     ap.add_argument("--impl", default="mako", choices=["mako", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

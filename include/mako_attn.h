@@ -197,6 +197,18 @@ int mako_heads_partial(mako_attn_ctx* ctx, void* stream, int dtype, const float*
 int mako_heads_clear(mako_attn_ctx* ctx, void* stream, int dtype, void* y, uint32_t dim, uint32_t n_pad, uint32_t from,
                      uint32_t heads);
 
+/* ---- The consumer of the attention's output --------------------------------------------------------------------- */
+
+/* The output projection: y[t][j] = sum_i x[t][i] * w[j][i] for x [T][k] (the attention's o in its 16-bit form,
+ * MAKO_OPT_OUTPUT_16BIT) and the matrix w [n][k] (one output row per j), both of `dtype`, accumulated in fp32 into
+ * y [T][ldy] floats (ldy 0: n).  Replaces Runtime::proj (src/gpu/runtime.cpp:164-190) for BF16 / F16 matrices, which
+ * the reference calls right after the attention (src/models/h3.cpp:366, src/models/qwen_text.cpp:312) and which
+ * rounds the fp32 o to 16 bits first (the attention's 16-bit output does that rounding in its epilogue, the same
+ * round-to-nearest-even).  Same rejection as the reference: k a multiple of 64; also 16-byte aligned tensors and ldy a
+ * multiple of 4.  sm_100 only (MAKO_ENOTSUP otherwise). */
+int mako_proj(mako_attn_ctx* ctx, void* stream, int dtype, const void* w, const void* x, float* y, uint32_t T,
+              uint32_t k, uint32_t n, uint32_t ldy);
+
 /* ---- Multi-GPU: one process per GPU of one box, the peers' memory mapped through CUDA IPC ------------------------
  * No reference counterpart: mako-common drives one Apple GPU.  BASELINE's sharded forms -- heads across GPUs with the
  * outputs gathered, and one long sequence's KV cache across GPUs with a log-sum-exp combine -- are built from these.

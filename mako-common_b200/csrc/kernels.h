@@ -139,4 +139,14 @@ struct CubeParams {
 };
 cudaError_t launch_cube_select(const CubeParams& p, int dtype, cudaStream_t s);
 
+// The output projection after the attention: y[t][j] = sum_i x[t][i] w[j][i], x [T][k] and w [n][k] 16-bit (one type),
+// y [T][ldy] fp32; k a multiple of 64.
+struct ProjParams {
+    const void* x;
+    const void* w;
+    float* y;
+    uint32_t T, k, n, ldy, num_sms;
+};
+cudaError_t launch_proj_gemm(const ProjParams& p, int dtype, int* err, cudaStream_t s);
+
 } // namespace mako

@@ -785,6 +785,42 @@ int mako_heads_partial(mako_attn_ctx* ctx, void* stream, int dtype, const float*
     return heads_common(ctx, stream, dtype, p, "heads_partial");
 }
 
+int mako_proj(mako_attn_ctx* ctx, void* stream, int dtype, const void* w, const void* x, float* y, uint32_t T,
+              uint32_t k, uint32_t n, uint32_t ldy)
+{
+    if (int rc = check_ctx(ctx, dtype))
+        return rc;
+    if (k % 64)  // the reference's own limit for its BF16 GEMM (src/gpu/runtime.cpp:178-179)
+        return fail(MAKO_EINVAL, "BF16 %ux%u: k must be a multiple of 64", k, n);
+    if (ldy == 0)
+        ldy = n;
+    if (ldy < n || !w || !x || !y || !aligned16(w) || !aligned16(x) || !aligned16(y) || ldy % 4)
+        return fail(MAKO_EINVAL, "proj: null or unaligned tensor, or row stride %u under %u (16-byte aligned rows)", ldy,
+                    n);
+    if (ctx->cc_major != 10)
+        return fail(MAKO_ENOTSUP, "proj: the tcgen05 GEMM needs sm_100 (sm_%d)", ctx->cc_major * 10);
+    if (T == 0 || n == 0)
+        return MAKO_OK;
+    DeviceGuard dg(ctx->device);
+    if (dg.err != cudaSuccess)
+        return cuda_fail("set device", dg.err);
+    mako::ProjParams p{};
+    p.x = x;
+    p.w = w;
+    p.y = y;
+    p.T = T;
+    p.k = k;
+    p.n = n;
+    p.ldy = ldy;
+    p.num_sms = uint32_t(ctx->num_sms);
+    auto st = static_cast<cudaStream_t>(stream);
+    ctx->launches += 1;
+    KernelTimer t(ctx, st);
+    cudaError_t e = mako::launch_proj_gemm(p, dtype, ctx->err, st);
+    t.stop();
+    return launched("proj", e);
+}
+
 int mako_heads_clear(mako_attn_ctx* ctx, void* stream, int dtype, void* y, uint32_t dim, uint32_t n_pad, uint32_t from,
                      uint32_t heads)
 {

@@ -24,7 +24,7 @@ SYMBOLS = (
     "mako_peer_alloc", "mako_peer_free", "mako_peer_open", "mako_peer_close", "mako_group_create", "mako_group_connect",
     "mako_group_destroy", "mako_attention_gather", "mako_attention_decode_kv_sharded", "mako_group_connect_ptrs",
     "mako_group_area", "mako_heads", "mako_heads_norm", "mako_heads_partial", "mako_heads_clear",
-    "mako_cube_layout",
+    "mako_cube_layout", "mako_proj",
 )
 
 
@@ -78,6 +78,7 @@ def lib():
     L.mako_heads_norm.argtypes = [p, p, i32, p, u32, u32, u32, u32, u32, p, u32, p, f32, u32, p]
     L.mako_heads_partial.argtypes = [p, p, i32, p, u32, u32, u32, u32, u32, u32, u32, u32, p, p, f32, p, p]
     L.mako_heads_clear.argtypes = [p, p, i32, p, u32, u32, u32, u32]
+    L.mako_proj.argtypes = [p, p, i32, p, p, p, u32, u32, u32, u32]
     L.mako_cube_layout.argtypes = [u32] * 6 + [ctypes.c_float, p, p, p, ctypes.POINTER(CubeLayoutInfo)]
     H = ctypes.POINTER(IpcHandle)
     L.mako_peer_alloc.argtypes = [p, ctypes.c_size_t, ctypes.POINTER(p), H]
@@ -197,6 +198,10 @@ class Context:
 
     # -- TransformerRuntime::heads / heads_norm / heads_partial (src/models/runtime.cpp:215-260) and heads_clear;
     # y is a float16 or bfloat16 tensor [heads][n_pad][dim], x / cs / w float32 tensors (cs: (cos, sin) pairs)
+    def proj(self, w, x, y, T, k, n, ldy=0, stream=None):
+        """mako_proj: y[t][j] = sum_i x[t][i] w[j][i] (x [T][k], w [n][k] 16-bit of one type, y fp32 [T][ldy])."""
+        _check(lib().mako_proj(self._h, _stream(stream), dtype_code(x), _ptr(w), _ptr(x), _ptr(y), T, k, n, ldy))
+
     def heads(self, x, ld, col0, heads, T, n_pad, cs, rope, y, stream=None):
         _check(lib().mako_heads(self._h, _stream(stream), dtype_code(y), _ptr(x), ld, col0, heads, T, n_pad, _ptr(cs),
                                 rope, _ptr(y)))

@@ -404,4 +404,33 @@ void oracle_heads(const float* x, uint64_t ld, uint32_t col0, uint32_t stride, u
         }
 }
 
+// The output projection (Runtime::proj on a 16-bit matrix, src/gpu/runtime.cpp:164-190): y[t][j] = sum_i x[t][i]
+// w[j][i] in double over the 16-bit x [T][k] and w [n][k] (x is what the reference's to_bf16 / to_half makes of the
+// fp32 attention output), y [T][ldy] floats.  rows: the t to compute (null: all), n_rows of them.
+void oracle_proj(int dtype, const uint16_t* w, const uint16_t* x, float* y, uint32_t T, uint32_t k, uint32_t n,
+                 uint32_t ldy, const uint32_t* rows, uint32_t n_rows, int threads)
+{
+    set_threads(threads);
+    const uint32_t nr = rows ? n_rows : T;
+    std::vector<double> wd(uint64_t(n) * k);
+    for (uint64_t i = 0; i < wd.size(); ++i)
+        wd[i] = widen(w[i], dtype);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t r = 0; r < int64_t(nr); ++r) {
+        const uint32_t t = rows ? rows[r] : uint32_t(r);
+        if (t >= T)
+            continue;
+        std::vector<double> xd(k);
+        for (uint32_t i = 0; i < k; ++i)
+            xd[i] = widen(x[uint64_t(t) * k + i], dtype);
+        for (uint32_t j = 0; j < n; ++j) {
+            const double* wr = &wd[uint64_t(j) * k];
+            double s = 0;
+            for (uint32_t i = 0; i < k; ++i)
+                s += xd[i] * wr[i];
+            y[uint64_t(t) * ldy + j] = float(s);
+        }
+    }
+}
+
 } // extern "C"

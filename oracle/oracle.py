@@ -42,6 +42,8 @@ def lib():
         L.oracle_sparse_test_fixture.argtypes = [ptr] * 6
         L.oracle_heads.argtypes = [ptr, ctypes.c_uint64] + [u32] * 9 + [ptr, u32, ptr, ctypes.c_float, ptr, ptr]
         L.oracle_heads.restype = None
+        L.oracle_proj.argtypes = [i32, ptr, ptr, ptr] + [u32] * 4 + [ptr, u32, i32]
+        L.oracle_proj.restype = None
         for f in (L.oracle_attention, L.oracle_decode, L.oracle_attention_sparse, L.oracle_cube_select,
                   L.oracle_sparse_test_fixture):
             f.restype = None
@@ -227,4 +229,14 @@ def heads(x, ld, col0, stride, dim, rot, rope, rows, heads_, n_pad, row0=0, cs=N
     m = None if map_ is None else _c(map_, np.int32)
     lib().oracle_heads(_p(x), ld, col0, stride, dim, rot, rope, rows, heads_, n_pad, row0, _p(cs), cs_row, _p(w),
                        eps, _p(m), _p(y))
+    return y
+
+
+def proj(dtype, w, x, T, k, n, rows=None, nthreads=0):
+    """The output projection in double: y [T][n] float32 (rows not in `rows` left 0) from 16-bit patterns x [T][k]
+    and w [n][k]."""
+    w, x = _c(w, np.uint16), _c(x, np.uint16)
+    y = np.zeros((T, n), np.float32)
+    r = None if rows is None else _c(rows, np.uint32)
+    lib().oracle_proj(dtype, _p(w), _p(x), _p(y), T, k, n, n, _p(r), 0 if r is None else len(r), nthreads)
     return y

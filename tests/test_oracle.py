@@ -215,3 +215,17 @@ def test_heads_oracle_matches_numpy(oracle):
     np.testing.assert_allclose(yq[0][:, 1::2], x[:, 0:64:2], atol=1e-6)
     yn = oracle.heads(x, ld, 0, 64, 64, 0, 0, T, 1, T, w=np.ones(64, np.float32), eps=1e-12)
     np.testing.assert_allclose(np.sqrt((yn[0].astype(np.float64) ** 2).mean(-1)), 1.0, rtol=1e-6)
+
+
+def test_proj_restatement(oracle):
+    """The oracle's double GEMM against numpy's float64 product of the same 16-bit values."""
+    rng = np.random.default_rng(5)
+    for dtype in (0, 1):
+        x = oracle.to_bits(rng.standard_normal((37, 128)).astype(np.float32), dtype)
+        w = oracle.to_bits(rng.standard_normal((45, 128)).astype(np.float32), dtype)
+        want = oracle.from_bits(x, dtype).astype(np.float64) @ oracle.from_bits(w, dtype).astype(np.float64).T
+        got = oracle.proj(dtype, w, x, 37, 128, 45)
+        assert np.allclose(got, want.astype(np.float32), rtol=1e-6, atol=1e-6)
+        rows = np.array([3, 30], np.uint32)
+        part = oracle.proj(dtype, w, x, 37, 128, 45, rows=rows)
+        assert np.array_equal(part[rows], got[rows]) and not np.any(part[5])
