@@ -66,6 +66,12 @@ public:
         check(mako_attention_decode(ctx_, stream_, dtype_, q, k, v, o, batch, kv_len, max_kv_len, heads, kv_heads, dim,
                                     k_stride));
     }
+    // Runtime::proj for a BF16 / F16 matrix (src/gpu/runtime.cpp:164-190) on the attention's 16-bit output:
+    // y[t][j] = sum_i x[t][i] w[j][i], x [T][k] and w [n][k] of this object's dtype, y [T][ldy] floats (0: n).
+    void proj(const void* w, const void* x, float* y, uint32_t T, uint32_t k, uint32_t n, uint32_t ldy = 0)
+    {
+        check(mako_proj(ctx_, stream_, dtype_, w, x, y, T, k, n, ldy));
+    }
     // TransformerRuntime::heads_partial (src/models/runtime.hpp:82-87): y 16-bit tiles of this object's dtype.
     void heads_partial(const float* x, uint32_t ld, uint32_t col0, uint32_t stride, uint32_t dim, uint32_t rot,
                        uint32_t heads, uint32_t T, uint32_t n_pad, const float* cs, const float* w, float eps, void* y,
