@@ -39,9 +39,7 @@ constexpr uint32_t HBOX = 64 * 64 * 2;   // a 64-row x 64-value TMA box: 8 KB
 constexpr uint32_t STILE = 2 * DBOX;     // 128 rows x 128 values
 constexpr uint32_t S_Q = 0, S_K = STILE, S_V = S_K + NSK * STILE, S_BAR = S_V + NSV * STILE;
 constexpr uint32_t S_STAT = S_BAR + 256;   // float2 [2 parities][128 rows]: each parity's (max, sum) per row
-constexpr uint32_t kListCache = 1024;        // list entries per cube kept in shared memory
-constexpr uint32_t S_LIST = S_STAT + 2048;  // uint32 [2 cubes][kListCache]
-constexpr uint32_t S_TOTAL = S_LIST + 2 * kListCache * 4 + 1024;
+constexpr uint32_t S_TOTAL = S_STAT + 2048 + 1024;
 constexpr uint32_t COL_O = 256;  // O of parity x at COL_O + 128 x; S (and the P that replaces it) of parity x at 128 x
 constexpr long long S_WAIT_LIMIT = 1ll << 31;
 
@@ -73,7 +71,24 @@ __device__ __forceinline__ uint32_t list_entry(const SpParams& p, const void* ba
                      : uint32_t(__ldg(static_cast<const uint16_t*>(base) + i));
 }
 
-__device__ __forceinline__ TileInfo tile_info(const SpParams& p, uint32_t u, uint32_t h)
+// A tile's list lengths as read from nsel (two cubes; 0 past the cubes), loaded without being used, so that a caller
+// can issue the loads early and build the TileInfo later (tile_from).
+struct TileRaw {
+    int64_t n[2];
+};
+__device__ __forceinline__ TileRaw tile_raw(const SpParams& p, uint32_t u, uint32_t h)
+{
+    TileRaw r{{0, 0}};
+    if (u < p.tiles_cube)
+        for (uint32_t hh = 0; hh < 2; ++hh) {
+            const uint32_t c = 2 * u + hh;
+            if (c < p.n_cubes)
+                r.n[hh] = p.sel_i32 ? int64_t(static_cast<const int32_t*>(p.nsel)[uint64_t(h) * p.n_cubes + c])
+                                    : int64_t(static_cast<const uint16_t*>(p.nsel)[uint64_t(h) * p.n_cubes + c]);
+        }
+    return r;
+}
+__device__ __forceinline__ TileInfo tile_from(const SpParams& p, uint32_t u, const TileRaw& r)
 {
     TileInfo t{};
     if (u >= p.tiles_total)
@@ -85,13 +100,8 @@ __device__ __forceinline__ TileInfo tile_info(const SpParams& p, uint32_t u, uin
         for (uint32_t hh = 0; hh < 2; ++hh) {
             const uint32_t c = 2 * u + hh;
             t.cube_id[hh] = c;
-            uint32_t n = 0;
-            if (c < p.n_cubes) {
-                const int64_t raw = p.sel_i32 ? int64_t(static_cast<const int32_t*>(p.nsel)[uint64_t(h) * p.n_cubes + c])
-                                              : int64_t(static_cast<const uint16_t*>(p.nsel)[uint64_t(h) * p.n_cubes + c]);
-                n = raw <= 0 ? 0u : (raw < int64_t(p.max_sel) ? uint32_t(raw) : p.max_sel);
-            }
-            t.ns[hh] = n;
+            const int64_t raw = c < p.n_cubes ? r.n[hh] : 0;
+            t.ns[hh] = raw <= 0 ? 0u : (raw < int64_t(p.max_sel) ? uint32_t(raw) : p.max_sel);
         }
         t.ncp = max(t.ns[0], t.ns[1]);
         t.np = t.ncp + (p.dense1 > p.dense0 ? (p.dense1 - p.dense0 + 127) / 128 : 0);
@@ -100,6 +110,10 @@ __device__ __forceinline__ TileInfo tile_info(const SpParams& p, uint32_t u, uin
         t.np = (p.n_k + 127) / 128;
     }
     return t;
+}
+__device__ __forceinline__ TileInfo tile_info(const SpParams& p, uint32_t u, uint32_t h)
+{
+    return tile_from(p, u, tile_raw(p, u, h));
 }
 
 // The list entry a cube pass reads (pass pi, half hh), or 0xFFFFFFFF when the list has no entry there; read well
@@ -362,7 +376,6 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         const uint32_t tl = tmem + ((qd * 32) << 16);
         const uint32_t colS = 128 * x, colO = COL_O + 128 * x;
         float2* const stat = reinterpret_cast<float2*>(gbase + S_STAT);
-        uint32_t* const lcache = reinterpret_cast<uint32_t*>(gbase + S_LIST);
         const float scale = p.scale_log2;
         const uint64_t scale2 = pack2(scale, scale);
         bool ok = true;
@@ -370,23 +383,19 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         // Every softmax thread walks all of its CTA's items, also after a failed wait (then without waiting or
         // computing), so that the two parities keep meeting at the named barriers, which cannot time out.  An item
         // without passes (no key at all) stores zeros.
-        for (uint32_t round = 0;; ++round) {
-            const uint32_t ii = sp_item(round);
-            if (ii >= n_items)
-                break;
-            uint32_t h, kvh;
-            const TileInfo t = item(ii, h, kvh);
-            // this item's cube lists, copied to shared memory once (the passes read them without global-load
-            // latency); the first barrier also keeps a fast thread from overwriting entries a slow one still reads
-            const bool cached = t.cube && t.ncp <= kListCache;
-            named_bar(5, 256);
-            if (cached)
-                for (uint32_t k = threadIdx.x - 128; k < 2 * kListCache; k += 256) {
-                    const uint32_t hh = k / kListCache, pi = k % kListCache;
-                    if (pi < t.ncp)
-                        lcache[k] = raw_entry(p, t, h, pi, hh);
-                }
-            named_bar(5, 256);
+        // The next item's list lengths and its first list entry are loaded one item ahead (before the current
+        // item's epilogue), so an item's start does not wait on global memory.
+        auto unit = [&](uint32_t i) { return p.tiles_total - 1 - i % p.tiles_total; };
+        auto entry_of = [&](const TileInfo& tt, uint32_t hh_, uint32_t pi) {
+            return tt.cube && pi < tt.ncp ? raw_entry(p, tt, hh_, pi, hr) : 0u;
+        };
+        uint32_t ii = sp_item(0);
+        TileInfo t = ii < n_items ? tile_info(p, unit(ii), ii / p.tiles_total) : TileInfo{};
+        uint32_t raw_next = ii < n_items ? entry_of(t, ii / p.tiles_total, (g & 1) == x ? 0u : 1u) : 0u;
+        for (uint32_t round = 0; ii < n_items; ++round) {
+            const uint32_t h = ii / p.tiles_total, kvh = h / (p.heads / p.kv_heads);
+            const uint32_t ii_n = sp_item(round + 1);
+            const TileRaw rn = ii_n < n_items ? tile_raw(p, unit(ii_n), ii_n / p.tiles_total) : TileRaw{{0, 0}};
             float m = -INFINITY, l = 0.0f;
             uint32_t mine = 0;  // passes of this parity in the item
 
@@ -476,15 +485,18 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                     mbar_arrive_n(p_full(x), 1);
             };
 
-            for (uint32_t pi = 0; pi < t.np; ++pi) {
+            // This thread's list entry (its cube's) for each of this parity's cube passes, read one pass of the
+            // parity (two passes) ahead so that the load's latency hides behind a pass.
+            auto entry = [&](uint32_t pi) { return entry_of(t, h, pi); };
+            const uint32_t first = ((g & 1) == x) ? 0u : 1u;  // this parity's first pass of the item
+            for (uint32_t pi = first; pi < t.np; pi += 2) {
                 const uint32_t gi = g + pi;
-                if ((gi & 1) != x)
-                    continue;
+                const uint32_t raw = raw_next;
+                if (pi + 2 < t.np)
+                    raw_next = entry(pi + 2);
                 const bool half = t.cube && pi < t.ncp;  // this row sees only its cube's 64 keys
                 uint32_t j0, hi;
-                const uint32_t hh = half ? hr : 0;
-                keys_of(p, t, pi, hh,
-                        half ? (cached ? lcache[hh * kListCache + pi] : raw_entry(p, t, h, pi, hh)) : 0u, j0, hi);
+                keys_of(p, t, pi, half ? hr : 0, half ? raw : 0u, j0, hi);
                 if (ok)
                     ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), (gi >> 1) & 1, S_WAIT_LIMIT));
                 if (ok && (threadIdx.x & 127) == 0) {
@@ -508,6 +520,9 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             }
             nd += mine > 0;
             g += t.np;
+            // the next item, and its first entry for this parity, before this item's epilogue
+            const TileInfo tn = ii_n < n_items ? tile_from(p, unit(ii_n), rn) : TileInfo{};
+            raw_next = ii_n < n_items ? entry_of(tn, ii_n / p.tiles_total, (g & 1) == x ? 0u : 1u) : 0u;
             // Merge the parities: exchange (max, sum) with the other parity's thread of this row, then this thread
             // stores output columns [64 x, 64 x + 64) from both parities' O.
             stat[x * 128 + row] = make_float2(mine > 0 ? m : -INFINITY, mine > 0 ? l : 0.0f);
@@ -547,6 +562,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             fence_before();
             named_bar(1 + qd, 64);
             fence_after();
+            ii = ii_n;
+            t = tn;
         }
         if (!ok && lane == 0)
             atomicExch(p.err, 13);
