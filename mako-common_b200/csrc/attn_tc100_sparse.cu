@@ -39,13 +39,15 @@ constexpr uint32_t HBOX = 64 * 64 * 2;   // a 64-row x 64-value TMA box: 8 KB
 constexpr uint32_t STILE = 2 * DBOX;     // 128 rows x 128 values
 constexpr uint32_t S_Q = 0, S_K = STILE, S_V = S_K + NSK * STILE, S_BAR = S_V + NSV * STILE;
 constexpr uint32_t S_STAT = S_BAR + 256;   // float2 [2 parities][128 rows]: each parity's (max, sum) per row
-constexpr uint32_t S_TOTAL = S_STAT + 2048 + 1024;
+constexpr uint32_t S_STAGE = (S_STAT + 2048 + 1023) / 1024 * 1024;  // 2 KB per softmax warp: 32 rows x 16 floats
+constexpr uint32_t S_TOTAL = S_STAGE + 8 * 2048 + 1024;
 constexpr uint32_t COL_O = 256;  // O of parity x at COL_O + 128 x; S (and the P that replaces it) of parity x at 128 x
 constexpr long long S_WAIT_LIMIT = 1ll << 31;
 
 struct __align__(64) SpParams {
     CUtensorMap tk, tv;  // k and v (or the fp16 copy of v), 64-row boxes
     CUtensorMap tq;      // q, 128-row boxes
+    CUtensorMap to;      // o [n_q][width] fp32, boxes of 32 rows x 16 floats (64-byte swizzle), when use_tma_out
     const void* q;
     float* o;
     int* err;
@@ -54,7 +56,7 @@ struct __align__(64) SpParams {
     const void* nsel;
     const uint8_t* valid;
     const int32_t* map;
-    uint32_t sel_i32, qk_fmt, o_type;
+    uint32_t sel_i32, qk_fmt, o_type, use_tma_out;
     uint32_t n_q, q_pad, n_k, k_pad, heads, kv_heads, width, n_cubes, max_sel, dense0, dense1;
     uint32_t tiles_cube, tiles_total;
     float scale_log2;
@@ -541,6 +543,10 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             }
             const float inv = (L > 0.0f ? 1.0f / L : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
             const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * x;
+            // identity rows and fp32 o: the warp stores its rows by TMA (rows past n_q are clipped by the tensor
+            // map); a cube tile's half past the last cube belongs to another tile and is not written
+            const bool tma_out = p.use_tma_out && t.active && (!t.cube || t.cube_id[hr] < p.n_cubes);
+            const uint32_t stage = base + S_STAGE + (warp - 4) * 2048;
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
                 // both parities' columns (warp-collective loads; a parity without passes in this item holds an older
@@ -555,8 +561,34 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 for (int e = 0; e < 32; ++e)
                     o[e] = __float_as_uint((has0 ? __uint_as_float(o[e]) * w0 : 0.0f) +
                                            (has1 ? __uint_as_float(o1[e]) * w1 : 0.0f));
-                if (store)
+                if (tma_out) {
+                    // the warp's 32 rows x 16 columns at a time through its staging buffer (row = lane, 16-byte
+                    // chunks in the 64-byte swizzle's order), stored by one TMA box; the thread does not wait on
+                    // 32 scattered row stores
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        if (lane == 0)
+                            bulk_wait_read0();  // the previous box has been read out of the buffer
+                        __syncwarp();
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(
+                                             stage + lane * 64 + ((c ^ ((lane >> 1) & 3)) * 16)),
+                                         "f"(__uint_as_float(o[16 * hf + 4 * c]) * inv),
+                                         "f"(__uint_as_float(o[16 * hf + 4 * c + 1]) * inv),
+                                         "f"(__uint_as_float(o[16 * hf + 4 * c + 2]) * inv),
+                                         "f"(__uint_as_float(o[16 * hf + 4 * c + 3]) * inv)
+                                         : "memory");
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&p.to, stage, int(h * SD + 64 * x + 32 * k + 16 * hf), int(t.row0 + 32 * qd));
+                            bulk_commit();
+                        }
+                    }
+                } else if (store) {
                     out_store32(p.o, orow + 32 * k, o, inv, p.o_type);
+                }
             }
             // both parities' O (and the stat entries) are read before either parity's next item writes them
             fence_before();
@@ -567,6 +599,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         }
         if (!ok && lane == 0)
             atomicExch(p.err, 13);
+        if (lane == 0)
+            bulk_wait0();  // this warp's output boxes have landed
     }
     __syncwarp();
     fence_before();
@@ -592,6 +626,21 @@ cudaError_t launch_attn_tc_sparse(const AttnParams& a, int dtype, bool sel_i32, 
         return cudaErrorInvalidValue;
     p.q = a.q;
     p.o = a.o;
+    p.use_tma_out = 0;
+    if (a.o_type == 0 && !a.map) {  // identity rows, fp32: the epilogue stores by TMA
+        auto enc = tensor_map_encoder();
+        if (!enc)
+            return cudaErrorInvalidValue;
+        cuuint64_t dims[2] = {a.width, a.n_q};
+        cuuint64_t strides[1] = {uint64_t(a.width) * 4};
+        cuuint32_t box[2] = {16, 32};
+        cuuint32_t estr[2] = {1, 1};
+        if (enc(&p.to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.o, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+        p.use_tma_out = 1;
+    }
     p.err = err;
     p.vinv = bf ? vinv : nullptr;
     p.sel = a.sel;
