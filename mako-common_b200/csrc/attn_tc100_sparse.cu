@@ -10,16 +10,14 @@
 // partner's is padded with empty passes; an entry >= n_cubes is skipped.  Masking per key: valid[key] and the pass's
 // key range (ops.metal:1109); output row r goes to o row map[r], dropped when < 0 (ops.metal:1174-1184).
 //
-// One tile per CTA (384 threads): warp 0 loads the tile's Q once and the K ring, warp 2 the V ring (TMA, 64-row boxes
-// for K and V so each half can come from anywhere; K in a 2-stage ring, V in a 3-stage ring), warp 1 issues UMMA, and
-// warps 4-11 run the softmax and the epilogue: each query row (TMEM lane) belongs to one thread of warps 4-7 and one
-// of warps 8-11, which take half of the row's columns each and agree on the row maximum through shared memory, so
-// two warps per sub-partition share the exp unit.
-// TMEM (512 columns): S in two buffers (0-127, 128-255), O (256-383) and P in two buffers (384-447, 448-511, fp16
-// pairs, the A operand of P.V); Q.K^T reads Q and K from shared memory.  The issue order is QK(0), QK(1), then per
-// pass PV(i), QK(i + 2): Q K^T(i + 2) waits only until the softmax has read S(i), and the softmax writes P(i) into
-// the buffer P.V(i - 2) read (finished before Q K^T(i), committed after it), so it waits for a product only to
-// rescale O.  Precision, bounded waits and the error flag as the dense kernel (attn_tc100.cu).
+// A persistent grid (one CTA of 384 threads per SM) works through (tile, head) items head by head.  Warp 0 loads each
+// item's Q once and the K ring, warp 2 the V ring (TMA, 64-row boxes for K and V so each half can come from anywhere;
+// K in a 2-stage ring, V in a 3-stage ring), warp 1 issues UMMA, and warps 4-11 run the softmax and the epilogue:
+// each query row (TMEM lane) belongs to one thread of warps 4-7 (parity 0) and one of warps 8-11 (parity 1), which
+// take alternate passes.  TMEM (512 columns): S of parity x in columns 128 x .. 128 x + 127 (its P, fp16 pairs,
+// written over the first 64), one O accumulator (256-383) and the item's Q (384-447, the A operand of Q.K^T, copied
+// there by the softmax threads from the TMA tile).  The issue order is QK(0), QK(1), then per pass PV(i), QK(i + 2).
+// Precision, bounded waits and the error flag as the dense kernel (attn_tc100.cu).
 #include "common.cuh"
 #include "kernels.h"
 #include "tc100.cuh"
@@ -38,10 +36,12 @@ constexpr uint32_t DBOX = 128 * 64 * 2;  // one d-half of a 128-row tile: 16 KB
 constexpr uint32_t HBOX = 64 * 64 * 2;   // a 64-row x 64-value TMA box: 8 KB
 constexpr uint32_t STILE = 2 * DBOX;     // 128 rows x 128 values
 constexpr uint32_t S_Q = 0, S_K = STILE, S_V = S_K + NSK * STILE, S_BAR = S_V + NSV * STILE;
-constexpr uint32_t S_STAT = S_BAR + 256;   // float2 [2 parities][128 rows]: each parity's (max, sum) per row
-constexpr uint32_t S_STAGE = (S_STAT + 2048 + 1023) / 1024 * 1024;  // 2 KB per softmax warp: 32 rows x 16 floats
+constexpr uint32_t S_STAT = S_BAR + 256;   // float2 [2 parities][128 rows]: each thread's (maximum, sum share)
+constexpr uint32_t S_MAX = S_STAT + 2048;  // float [128 rows]: the running maximum handed between the parities
+constexpr uint32_t S_STAGE = (S_MAX + 512 + 1023) / 1024 * 1024;  // 2 KB per softmax warp: 32 rows x 16 floats
 constexpr uint32_t S_TOTAL = S_STAGE + 8 * 2048 + 1024;
-constexpr uint32_t COL_O = 256;  // O of parity x at COL_O + 128 x; S (and the P that replaces it) of parity x at 128 x
+// TMEM columns: S (and the P that replaces it) of parity x at 128 x, O at COL_O, Q (bf16 or fp16 pairs) at COL_Q
+constexpr uint32_t COL_O = 256, COL_Q = 384;
 constexpr long long S_WAIT_LIMIT = 1ll << 31;
 
 struct __align__(64) SpParams {
@@ -184,13 +184,15 @@ __device__ __forceinline__ uint32_t sp_item(uint32_t round)
     return round * G + c;
 }
 
-// Passes alternate between two parities, each with its own S buffer and its own O accumulator and softmax
-// warpgroup: parity x takes the passes whose running number (over the CTA's items) has x as its low bit, and runs an
-// online softmax of its own over them (its own row maxima and sums).  The epilogue merges the two parities' (O, max,
-// sum) per row by log-sum-exp.  A pass's P replaces its S in place (P.V reads it from TMEM); Q.K^T of pass i + 2 into
-// the same buffer is issued right behind P.V(i): the tensor pipe executes one thread's MMAs in issue order.  So the
-// two parities' chains (softmax -> P.V -> Q.K^T -> softmax) interleave on the tensor core, and no row's softmax waits
-// for another thread.
+// Passes alternate between two softmax warpgroups ("parities"): parity x takes the passes whose running number (over
+// the CTA's items) has x as its low bit, each parity with its own S buffer (a pass's P replaces its S in place and
+// P.V reads it from TMEM).  Both parities accumulate into one O, so a row's running maximum is one sequence over the
+// item's passes, as in the reference: the thread that owns pass i takes the maximum pass i - 1 left (a named-barrier
+// hand-over between the two threads of the row), raises it when the pass's own maximum passes it by 8, hands it on,
+// and rescales O once the other parity's P.V(i - 1) has finished.  Each thread keeps its own share of the row sum,
+// relative to the maximum it last saw; the epilogue adds the two shares.  Q.K^T of pass i + 2 into the same S buffer
+// is issued right behind P.V(i): the tensor pipe executes one thread's MMAs in issue order.  Q sits in TMEM as the A
+// operand of Q.K^T, so Q.K^T reads only K from shared memory.
 __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_constant__ SpParams p)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -207,7 +209,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     auto o_done = [&](uint32_t x) { return sB + 128 + 8 * x; };  // the item's last P.V of parity x has finished
     const uint32_t q_full = sB + 152, mma_done = sB + 160;
     const uint32_t tmem_slot = sB + 168;
-    const uint32_t q_empty = sB + 176;  // an item's last Q.K^T has finished: Q may be overwritten
+    const uint32_t q_empty = sB + 176;  // an item's last Q.K^T has finished: TMEM's Q may be overwritten
+    const uint32_t q_tmem = sB + 184;   // the item's Q is in TMEM, and shared memory's Q buffer is free again
     volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -232,6 +235,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         }
         mbar_init(q_full, 1);
         mbar_init(q_empty, 1);
+        mbar_init(q_tmem, 8);  // one arrival per softmax warp
         mbar_init(mma_done, 1);
         fence_barrier_init();
     }
@@ -245,8 +249,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
     const uint32_t tmem = *tmem_slot_ptr;
 
     // Counters every role keeps alike: g counts the passes of the items so far (ring stages, parities and the phases
-    // of their barriers), nq the items with passes (Q loads and q_empty phases), nd[x] the items with a pass of
-    // parity x (o_done(x) phases).
+    // of their barriers), nq the items with passes (Q loads and copies, q_full / q_tmem / q_empty phases), nd[x] the
+    // items with a pass of parity x (o_done(x) phases).
     if (warp < 4) {
         // the producer / issuer warpgroup gives registers to the softmax warpgroups (384 x 168 at launch =
         // 128 x 104 + 256 x 200)
@@ -269,8 +273,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 const TileInfo t = item(i, h, kvh);
                 if (t.np == 0)
                     continue;
-                if (is_k) {  // the item's Q, once its predecessor's last Q.K^T has read the buffer
-                    if (nq > 0 && !mbar_wait(q_empty, (nq - 1) & 1, S_WAIT_LIMIT)) {
+                if (is_k) {  // the item's Q, once the softmax warps have copied the previous one into TMEM
+                    if (nq > 0 && !mbar_wait(q_tmem, (nq - 1) & 1, S_WAIT_LIMIT)) {
                         ok = false;
                         break;
                     }
@@ -312,8 +316,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 mbar_wait(is_k ? k_full(k % nst) : v_full(k % nst), (k / nst) & 1, S_WAIT_LIMIT);
         } else if (warp == 1 && lane == 0) {
             // ---------------- UMMA issuer ----------------
-            // Per item QK(0), QK(1), then per pass PV(i), QK(i + 2), both into parity i's buffers, one commit per
-            // Q.K^T; the K and V stages are released by a softmax thread that observes those completions anyway.
+            // Per item QK(0), QK(1), then per pass PV(i), QK(i + 2), one commit per Q.K^T; the K and V stages are
+            // released by a softmax thread that observes those completions anyway.
             const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, 128, 128);
             const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, 128, SD);
             auto qk = [&](uint32_t gj) {
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 fence_after();
 #pragma unroll
                 for (uint32_t ks = 0; ks < SD / 16; ++ks)
-                    umma_ss(tmem + x * 128, sdesc(base + S_Q + (ks >> 2) * DBOX + (ks & 3) * 32, 16, 1024),
+                    umma_ts(tmem + x * 128, tmem + COL_Q + ks * 8,
                             sdesc(base + S_K + s * STILE + (ks >> 2) * DBOX + (ks & 3) * 32, 16, 1024), idesc_qk,
                             ks > 0);
                 umma_commit(s_full(x));
@@ -339,7 +343,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 const TileInfo t = item(i, h, kvh);
                 if (t.np == 0)
                     continue;
-                ok = mbar_wait(q_full, nq & 1, S_WAIT_LIMIT);
+                ok = mbar_wait(q_tmem, nq & 1, S_WAIT_LIMIT);
                 ++nq;
                 fence_after();
                 ok = ok && qk(g) && (t.np < 2 || qk(g + 1));
@@ -354,8 +358,8 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                     fence_after();
 #pragma unroll
                     for (uint32_t kk = 0; kk < 8; ++kk)
-                        umma_ts(tmem + COL_O + 128 * x, tmem + 128 * x + kk * 8,
-                                sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024), idesc_pv, pi >= 2 || kk > 0);
+                        umma_ts(tmem + COL_O, tmem + 128 * x + kk * 8,
+                                sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024), idesc_pv, pi > 0 || kk > 0);
                     if (pi + 2 < t.np) {
                         ok = qk(gi + 2);
                         if (ok && pi + 3 == t.np)
@@ -376,14 +380,19 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         // ---------------- softmax of parity x and the epilogue: tile row `row` ----------------
         const uint32_t x = (warp - 4) >> 2, qd = warp & 3, row = qd * 32 + lane, hr = row >> 6;
         const uint32_t tl = tmem + ((qd * 32) << 16);
-        const uint32_t colS = 128 * x, colO = COL_O + 128 * x;
+        const uint32_t colS = 128 * x;
+        float* const mrow = reinterpret_cast<float*>(gbase + S_MAX);
         float2* const stat = reinterpret_cast<float2*>(gbase + S_STAT);
+        // named barriers of the row quadrant qd: 1 + 2 qd + y hands the running maximum to parity y's thread,
+        // 9 + qd pairs the two threads in the epilogue
+        const uint32_t bar_get = 1 + 2 * qd + x, bar_put = 1 + 2 * qd + (x ^ 1), bar_epi = 9 + qd;
         const float scale = p.scale_log2;
         const uint64_t scale2 = pack2(scale, scale);
         bool ok = true;
-        uint32_t g = 0, nd = 0;  // nd: items with a pass of this parity
+        uint32_t g = 0, nq = 0, nd0 = 0, nd1 = 0;
+        auto nd = [&](uint32_t y) { return y ? nd1 : nd0; };
         // Every softmax thread walks all of its CTA's items, also after a failed wait (then without waiting or
-        // computing), so that the two parities keep meeting at the named barriers, which cannot time out.  An item
+        // computing, but still meeting its partner at every named barrier, which cannot time out).  An item
         // without passes (no key at all) stores zeros.
         // The next item's list lengths and its first list entry are loaded one item ahead (before the current
         // item's epilogue), so an item's start does not wait on global memory.
@@ -391,19 +400,47 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         auto entry_of = [&](const TileInfo& tt, uint32_t hh_, uint32_t pi) {
             return tt.cube && pi < tt.ncp ? raw_entry(p, tt, hh_, pi, hr) : 0u;
         };
+        // Q of the next item with passes into TMEM: this thread's row, d-half x (64 values, two a column, the
+        // layout of an A operand), read from the 128-byte-swizzled tile TMA left in shared memory.
+        auto copy_q = [&]() {
+            if (ok && nq > 0)  // the previous item's last Q.K^T has read TMEM's Q
+                ok = __all_sync(0xffffffffu, mbar_wait(q_empty, (nq - 1) & 1, S_WAIT_LIMIT));
+            if (ok)
+                ok = __all_sync(0xffffffffu, mbar_wait(q_full, nq & 1, S_WAIT_LIMIT));
+            if (ok) {
+                fence_after();
+                uint32_t r[32];
+                const uint32_t src = base + S_Q + x * DBOX + row * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                                 : "=r"(r[4 * c]), "=r"(r[4 * c + 1]), "=r"(r[4 * c + 2]), "=r"(r[4 * c + 3])
+                                 : "r"(src + ((c ^ (row & 7)) * 16))
+                                 : "memory");
+                tmem_st32(tl + COL_Q + 32 * x, r);
+                tmem_wait_st();
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(q_tmem);
+            ++nq;
+        };
         uint32_t ii = sp_item(0);
         TileInfo t = ii < n_items ? tile_info(p, unit(ii), ii / p.tiles_total) : TileInfo{};
         uint32_t raw_next = ii < n_items ? entry_of(t, ii / p.tiles_total, (g & 1) == x ? 0u : 1u) : 0u;
+        bool q_in = false;  // the current item's Q was copied at the end of the previous item
         for (uint32_t round = 0; ii < n_items; ++round) {
             const uint32_t h = ii / p.tiles_total, kvh = h / (p.heads / p.kv_heads);
             const uint32_t ii_n = sp_item(round + 1);
             const TileRaw rn = ii_n < n_items ? tile_raw(p, unit(ii_n), ii_n / p.tiles_total) : TileRaw{{0, 0}};
-            float m = -INFINITY, l = 0.0f;
-            uint32_t mine = 0;  // passes of this parity in the item
+            if (t.np > 0 && !q_in)
+                copy_q();
+            float mref = -INFINITY, l = 0.0f;  // this thread's share of the row sum, relative to maximum mref
 
             // One pass of this parity: S (NK columns of this row from column c0) to P in place.  NK 64: a cube pass,
             // the row's own cube half (the other half's P is zero); NK 128: every column.
-            auto pass = [&](auto nk_tag, uint32_t c0, uint32_t key0, uint32_t hi) {
+            auto pass = [&](auto nk_tag, uint32_t pi, uint32_t gi, uint32_t c0, uint32_t key0, uint32_t hi) {
                 constexpr int NK = decltype(nk_tag)::value;
                 uint32_t r[NK / 32][32];
 #pragma unroll
@@ -423,13 +460,22 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                         mq[e] = max3f(mq[e], __uint_as_float(r[(c + 2 * e) >> 5][(c + 2 * e) & 31]),
                                       __uint_as_float(r[(c + 2 * e + 1) >> 5][(c + 2 * e + 1) & 31]));
                 const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
-                float f = 1.0f;
-                bool resc = false;
-                if (mx > m + 8.0f) {
-                    f = m == -INFINITY ? 0.0f : ex2(m - mx);
-                    m = mx;
-                    l *= f;
-                    resc = true;
+                // the running maximum after pass i - 1 (written by the other parity's thread of this row)
+                float mprev = -INFINITY;
+                if (pi > 0) {
+                    named_bar(bar_get, 64);
+                    mprev = mrow[row];
+                }
+                const float m = mx > mprev + 8.0f ? mx : mprev;
+                if (pi + 1 < t.np) {
+                    mrow[row] = m;
+                    named_arrive(bar_put, 64);
+                }
+                // O holds the earlier passes at maximum mprev; this thread's sum share at mref
+                const bool resc = m != mprev && mprev != -INFINITY;
+                if (m != mref) {
+                    l = mref == -INFINITY ? 0.0f : l * ex2(mref - m);
+                    mref = m;
                 }
                 const float mneg = m == -INFINITY ? 0.0f : -m;
                 const uint64_t mneg2 = pack2(mneg, mneg);
@@ -464,20 +510,24 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                     for (int k = 0; k < NK / 64; ++k)
                         tmem_st32(tl + colS + 32 * k, pk[k]);
                 }
-                // Rescale this parity's O before P.V adds to it: its previous product, P.V(i - 2), finished before
-                // S(i) was seen (the commit that signalled S(i) tracks it).
-                if (__any_sync(0xffffffffu, resc && mine > 0)) {
-                    const float gsc = resc ? f : 1.0f;
+                // Rescale O before P.V(i) adds to it, once the other parity's P.V(i - 1) has finished: the commit
+                // of Q.K^T(i + 1), issued after it, or the commit of that parity's last product of the item.
+                if (__any_sync(0xffffffffu, resc)) {
+                    const bool w = pi + 1 < t.np ? mbar_wait(s_full(x ^ 1), ((gi + 1) >> 1) & 1, S_WAIT_LIMIT)
+                                                 : mbar_wait(o_done(x ^ 1), nd(x ^ 1) & 1, S_WAIT_LIMIT);
+                    ok = __all_sync(0xffffffffu, w);
+                    fence_after();
+                    const float gsc = resc ? ex2(mprev - m) : 1.0f;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
+                    for (int k = 0; ok && k < 4; ++k) {
                         uint32_t o[32];
-                        tmem_ld32(tl + colO + 32 * k, o);
+                        tmem_ld32(tl + COL_O + 32 * k, o);
                         tmem_wait_ld();
                         reg_fence(o);
 #pragma unroll
                         for (int e = 0; e < 32; ++e)
                             o[e] = __float_as_uint(__uint_as_float(o[e]) * gsc);
-                        tmem_st32(tl + colO + 32 * k, o);
+                        tmem_st32(tl + COL_O + 32 * k, o);
                     }
                 }
                 tmem_wait_st();
@@ -510,30 +560,45 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 if (ok) {
                     fence_after();
                     if (half)
-                        pass(std::integral_constant<int, 64>{}, 64 * hr, j0, hi);
+                        pass(std::integral_constant<int, 64>{}, pi, gi, 64 * hr, j0, hi);
                     else
-                        pass(std::integral_constant<int, 128>{}, 0, j0, hi);
+                        pass(std::integral_constant<int, 128>{}, pi, gi, 0, j0, hi);
+                } else {  // no computing, but the hand-over of the maximum still pairs up
+                    if (pi > 0)
+                        named_bar(bar_get, 64);
+                    if (pi + 1 < t.np)
+                        named_arrive(bar_put, 64);
                 }
-                ++mine;
             }
-            if (ok && mine > 0) {  // this parity's O is final once its last P.V of the item lands
-                ok = __all_sync(0xffffffffu, mbar_wait(o_done(x), nd & 1, S_WAIT_LIMIT));
-                fence_after();
-            }
-            nd += mine > 0;
-            g += t.np;
             // the next item, and its first entry for this parity, before this item's epilogue
+            const uint32_t g0 = g;
+            g += t.np;
             const TileInfo tn = ii_n < n_items ? tile_from(p, unit(ii_n), rn) : TileInfo{};
             raw_next = ii_n < n_items ? entry_of(tn, ii_n / p.tiles_total, (g & 1) == x ? 0u : 1u) : 0u;
-            // Merge the parities: exchange (max, sum) with the other parity's thread of this row, then this thread
-            // stores output columns [64 x, 64 x + 64) from both parities' O.
-            stat[x * 128 + row] = make_float2(mine > 0 ? m : -INFINITY, mine > 0 ? l : 0.0f);
-            named_bar(1 + qd, 64);
+            // the next item's Q into TMEM now, so that its first products overlap this item's epilogue
+            q_in = tn.np > 0;
+            if (q_in)
+                copy_q();
+            if (ok && t.np > 0) {  // O is final once the item's last P.V has landed
+                const uint32_t xl = (g0 + t.np - 1) & 1;
+                ok = __all_sync(0xffffffffu, mbar_wait(o_done(xl), nd(xl) & 1, S_WAIT_LIMIT));
+                fence_after();
+            }
+            if (t.np > 0) {  // the parities with a pass in this item
+                nd0 += (g0 & 1) == 0 || t.np > 1;
+                nd1 += (g0 & 1) == 1 || t.np > 1;
+            }
+            // The row's sum: this thread's share and the other parity's thread's, each relative to the maximum
+            // it last saw (the larger of the two is the row's final maximum); this thread stores output columns
+            // [64 x, 64 x + 64).
+            stat[x * 128 + row] = make_float2(mref, l);
+            named_bar(bar_epi, 64);
             const float2 s0 = stat[row], s1 = stat[128 + row];
             const float M = fmaxf(s0.x, s1.x);
-            const float w0 = s0.x == -INFINITY ? 0.0f : ex2(s0.x - M), w1 = s1.x == -INFINITY ? 0.0f : ex2(s1.x - M);
-            const float L = s0.y * w0 + s1.y * w1;
-            const bool has0 = ok && s0.x != -INFINITY, has1 = ok && s1.x != -INFINITY;
+            const float L = M == -INFINITY ? 0.0f
+                                           : (s0.x == -INFINITY ? 0.0f : s0.y * ex2(s0.x - M)) +
+                                                 (s1.x == -INFINITY ? 0.0f : s1.y * ex2(s1.x - M));
+            const bool has = ok && t.np > 0 && M != -INFINITY;
             const uint32_t grow = t.row0 + row;
             bool store = t.active && grow < p.n_q && (!t.cube || t.cube_id[hr] < p.n_cubes);
             int64_t dst = grow;
@@ -549,18 +614,14 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             const uint32_t stage = base + S_STAGE + (warp - 4) * 2048;
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
-                // both parities' columns (warp-collective loads; a parity without passes in this item holds an older
-                // item's values, which the selects below leave out)
-                uint32_t o[32], o1[32];
+                // warp-collective load; an item without passes leaves an older item's values, replaced by zeros
+                uint32_t o[32];
                 tmem_ld32(tl + COL_O + 64 * x + 32 * k, o);
-                tmem_ld32(tl + COL_O + 128 + 64 * x + 32 * k, o1);
                 tmem_wait_ld();
                 reg_fence(o);
-                reg_fence(o1);
 #pragma unroll
                 for (int e = 0; e < 32; ++e)
-                    o[e] = __float_as_uint((has0 ? __uint_as_float(o[e]) * w0 : 0.0f) +
-                                           (has1 ? __uint_as_float(o1[e]) * w1 : 0.0f));
+                    o[e] = has ? o[e] : 0u;
                 if (tma_out) {
                     // the warp's 32 rows x 16 columns at a time through its staging buffer (row = lane, 16-byte
                     // chunks in the 64-byte swizzle's order), stored by one TMA box; the thread does not wait on
@@ -590,9 +651,9 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                     out_store32(p.o, orow + 32 * k, o, inv, p.o_type);
                 }
             }
-            // both parities' O (and the stat entries) are read before either parity's next item writes them
+            // O and the sum shares are read by both threads of the row before either starts the next item
             fence_before();
-            named_bar(1 + qd, 64);
+            named_bar(bar_epi, 64);
             fence_after();
             ii = ii_n;
             t = tn;

@@ -229,6 +229,12 @@ __device__ __forceinline__ void named_bar(uint32_t id, uint32_t count)
 {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
+// Arrives at named barrier `id` without waiting (the producer side: shared-memory writes before it are seen by the
+// threads that complete the barrier with named_bar).
+__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t count)
+{
+    asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
 
 // ---- packed fp32 arithmetic (sm_100) --------------------------------------------------------------------------------
 
