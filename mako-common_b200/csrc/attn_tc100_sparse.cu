@@ -437,6 +437,15 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             if (t.np > 0 && !q_in)
                 copy_q();
             float mref = -INFINITY, l = 0.0f;  // this thread's share of the row sum, relative to maximum mref
+            // the epilogue's global reads (v's scale, the row map) issued now, consumed after the passes
+            const float vscale = p.vinv ? p.vinv[kvh] : 1.0f;
+            const uint32_t grow = t.row0 + row;
+            bool store = t.active && grow < p.n_q && (!t.cube || t.cube_id[hr] < p.n_cubes);
+            int64_t dst = grow;
+            if (store && p.map) {
+                dst = p.map[grow];
+                store = dst >= 0;
+            }
 
             // One pass of this parity: S (NK columns of this row from column c0) to P in place.  NK 64: a cube pass,
             // the row's own cube half (the other half's P is zero); NK 128: every column.
@@ -599,14 +608,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                                            : (s0.x == -INFINITY ? 0.0f : s0.y * ex2(s0.x - M)) +
                                                  (s1.x == -INFINITY ? 0.0f : s1.y * ex2(s1.x - M));
             const bool has = ok && t.np > 0 && M != -INFINITY;
-            const uint32_t grow = t.row0 + row;
-            bool store = t.active && grow < p.n_q && (!t.cube || t.cube_id[hr] < p.n_cubes);
-            int64_t dst = grow;
-            if (store && p.map) {
-                dst = p.map[grow];
-                store = dst >= 0;
-            }
-            const float inv = (L > 0.0f ? 1.0f / L : 0.0f) * (p.vinv ? p.vinv[kvh] : 1.0f);
+            const float inv = (L > 0.0f ? 1.0f / L : 0.0f) * vscale;
             const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * x;
             // identity rows and fp32 o: the warp stores its rows by TMA (rows past n_q are clipped by the tensor
             // map); a cube tile's half past the last cube belongs to another tile and is not written
