@@ -40,8 +40,9 @@ constexpr uint32_t S_STAT = S_BAR + 256;   // float2 [2 parities][128 rows]: eac
 constexpr uint32_t S_MAX = S_STAT + 2048;  // float [128 rows]: the running maximum handed between the parities
 constexpr uint32_t S_STAGE = (S_MAX + 512 + 1023) / 1024 * 1024;  // 2 KB per softmax warp: 32 rows x 16 floats
 constexpr uint32_t S_TOTAL = S_STAGE + 8 * 2048 + 1024;
-// TMEM columns: S (and the P that replaces it) of parity x at 128 x, O at COL_O, Q (bf16 or fp16 pairs) at COL_Q
-constexpr uint32_t COL_O = 256, COL_Q = 384;
+// TMEM columns: S (and the P that replaces it) of parity x at 128 x, O at COL_O, Q (bf16 or fp16 pairs) at COL_Q,
+// and at COL_SPARE + 32 x the epilogue's parked output chunk of parity x
+constexpr uint32_t COL_O = 256, COL_Q = 384, COL_SPARE = 448;
 constexpr long long S_WAIT_LIMIT = 1ll << 31;
 
 struct __align__(64) SpParams {
@@ -320,9 +321,10 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             // released by a softmax thread that observes those completions anyway.
             const uint32_t idesc_qk = idesc_f16(p.qk_fmt, p.qk_fmt, 0, 0, 128, 128);
             const uint32_t idesc_pv = idesc_f16(0, 0, 0, 1, 128, SD);
-            auto qk = [&](uint32_t gj) {
+            // Q.K^T(gj) into parity gj's S; `seen`: K(gj) is known to have landed (a softmax thread waited for it)
+            auto qk = [&](uint32_t gj, bool seen) {
                 const uint32_t s = gj % NSK, x = gj & 1;
-                if (!mbar_wait(k_full(s), (gj / NSK) & 1, S_WAIT_LIMIT))
+                if (!seen && !mbar_wait(k_full(s), (gj / NSK) & 1, S_WAIT_LIMIT))
                     return false;
                 fence_after();
 #pragma unroll
@@ -346,13 +348,12 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 ok = mbar_wait(q_tmem, nq & 1, S_WAIT_LIMIT);
                 ++nq;
                 fence_after();
-                ok = ok && qk(g) && (t.np < 2 || qk(g + 1));
+                ok = ok && qk(g, false) && (t.np < 2 || qk(g + 1, false));
                 if (ok && t.np <= 2)
                     umma_commit(q_empty);
                 for (uint32_t pi = 0; ok && pi < t.np; ++pi) {
                     const uint32_t gi = g + pi, x = gi & 1, s = gi % NSV;
-                    ok = mbar_wait(p_full(x), (gi >> 1) & 1, S_WAIT_LIMIT) &&
-                         mbar_wait(v_full(s), (gi / NSV) & 1, S_WAIT_LIMIT);
+                    ok = mbar_wait(p_full(x), (gi >> 1) & 1, S_WAIT_LIMIT);  // P(i), V(i) and K(i + 2)
                     if (!ok)
                         break;
                     fence_after();
@@ -361,7 +362,7 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                         umma_ts(tmem + COL_O, tmem + 128 * x + kk * 8,
                                 sdesc(base + S_V + s * STILE + kk * 2048, DBOX, 1024), idesc_pv, pi > 0 || kk > 0);
                     if (pi + 2 < t.np) {
-                        ok = qk(gi + 2);
+                        ok = qk(gi + 2, true);  // K(i + 2) was waited for before P(i) was published
                         if (ok && pi + 3 == t.np)
                             umma_commit(q_empty);
                     } else {
@@ -430,6 +431,55 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
         TileInfo t = ii < n_items ? tile_info(p, unit(ii), ii / p.tiles_total) : TileInfo{};
         uint32_t raw_next = ii < n_items ? entry_of(t, ii / p.tiles_total, (g & 1) == x ? 0u : 1u) : 0u;
         bool q_in = false;  // the current item's Q was copied at the end of the previous item
+        // The epilogue reads this thread's 64 output columns out of O, stores the first 32 right away and parks the
+        // other 32 in spare TMEM columns (COL_SPARE + 32 x), so that O is free for the next item's first P.V sooner;
+        // the parked chunk is stored after this thread's next pass (pend: a chunk is parked).  The store metadata
+        // below belongs to the item whose output is being stored.
+        int pend = 0;
+        float p_inv = 0.0f;
+        uint64_t p_orow = 0;
+        bool p_tma = false, p_store = false;
+        uint32_t p_col = 0, p_row = 0;
+        const uint32_t stage = base + S_STAGE + (warp - 4) * 2048;
+        auto store_chunk = [&](int k, const uint32_t (&o)[32]) {
+            if (p_tma) {
+                // the warp's 32 rows x 16 columns at a time through its staging buffer (row = lane, 16-byte
+                // chunks in the 64-byte swizzle's order), stored by one TMA box
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    if (lane == 0)
+                        bulk_wait_read0();  // the previous box has been read out of the buffer
+                    __syncwarp();
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(
+                                         stage + lane * 64 + ((c ^ ((lane >> 1) & 3)) * 16)),
+                                     "f"(__uint_as_float(o[16 * hf + 4 * c]) * p_inv),
+                                     "f"(__uint_as_float(o[16 * hf + 4 * c + 1]) * p_inv),
+                                     "f"(__uint_as_float(o[16 * hf + 4 * c + 2]) * p_inv),
+                                     "f"(__uint_as_float(o[16 * hf + 4 * c + 3]) * p_inv)
+                                     : "memory");
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&p.to, stage, int(p_col + 32 * k + 16 * hf), int(p_row));
+                        bulk_commit();
+                    }
+                }
+            } else if (p_store) {
+                out_store32(p.o, p_orow + 32 * k, o, p_inv, p.o_type);
+            }
+        };
+        auto store_one = [&]() {
+            if (pend > 0) {
+                uint32_t pb[32];
+                tmem_ld32(tl + COL_SPARE + 32 * x, pb);
+                tmem_wait_ld();
+                reg_fence(pb);
+                store_chunk(1, pb);
+            }
+            pend = 0;
+        };
         for (uint32_t round = 0; ii < n_items; ++round) {
             const uint32_t h = ii / p.tiles_total, kvh = h / (p.heads / p.kv_heads);
             const uint32_t ii_n = sp_item(round + 1);
@@ -541,7 +591,12 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                 }
                 tmem_wait_st();
                 fence_before();
-                __syncwarp();
+                // P(i) is published once V(i) and K(i + 2) have landed too, so that the issuer waits on one barrier
+                // between P.V(i) and Q.K^T(i + 2) (both arrive well ahead; the waits cost the softmax time it has)
+                const bool vw = lane != 0 || (mbar_wait(v_full(gi % NSV), (gi / NSV) & 1, S_WAIT_LIMIT) &&
+                                              (pi + 2 >= t.np ||
+                                               mbar_wait(k_full((gi + 2) % NSK), ((gi + 2) / NSK) & 1, S_WAIT_LIMIT)));
+                ok = __all_sync(0xffffffffu, vw) && ok;
                 if (lane == 0)
                     mbar_arrive_n(p_full(x), 1);
             };
@@ -578,7 +633,10 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                     if (pi + 1 < t.np)
                         named_arrive(bar_put, 64);
                 }
+                store_one();  // the previous item's output, a chunk after each pass
             }
+            while (pend > 0)
+                store_one();
             // the next item, and its first entry for this parity, before this item's epilogue
             const uint32_t g0 = g;
             g += t.np;
@@ -608,58 +666,43 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
                                            : (s0.x == -INFINITY ? 0.0f : s0.y * ex2(s0.x - M)) +
                                                  (s1.x == -INFINITY ? 0.0f : s1.y * ex2(s1.x - M));
             const bool has = ok && t.np > 0 && M != -INFINITY;
-            const float inv = (L > 0.0f ? 1.0f / L : 0.0f) * vscale;
-            const uint64_t orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * x;
+            p_inv = (L > 0.0f ? 1.0f / L : 0.0f) * vscale;
+            p_orow = uint64_t(dst) * p.width + uint64_t(h) * SD + 64 * x;
             // identity rows and fp32 o: the warp stores its rows by TMA (rows past n_q are clipped by the tensor
             // map); a cube tile's half past the last cube belongs to another tile and is not written
-            const bool tma_out = p.use_tma_out && t.active && (!t.cube || t.cube_id[hr] < p.n_cubes);
-            const uint32_t stage = base + S_STAGE + (warp - 4) * 2048;
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                // warp-collective load; an item without passes leaves an older item's values, replaced by zeros
-                uint32_t o[32];
-                tmem_ld32(tl + COL_O + 64 * x + 32 * k, o);
+            p_tma = p.use_tma_out && t.active && (!t.cube || t.cube_id[hr] < p.n_cubes);
+            p_store = store;
+            p_col = h * SD + 64 * x;
+            p_row = t.row0 + 32 * qd;
+            // warp-collective loads; an item without passes leaves an older item's values, replaced by zeros.
+            // The first chunk is stored now, the second after this thread's next pass.
+            {
+                uint32_t pa[32], pb[32];
+                tmem_ld32(tl + COL_O + 64 * x, pa);
+                tmem_ld32(tl + COL_O + 64 * x + 32, pb);
                 tmem_wait_ld();
-                reg_fence(o);
+                reg_fence(pa);
+                reg_fence(pb);
 #pragma unroll
                 for (int e = 0; e < 32; ++e)
-                    o[e] = has ? o[e] : 0u;
-                if (tma_out) {
-                    // the warp's 32 rows x 16 columns at a time through its staging buffer (row = lane, 16-byte
-                    // chunks in the 64-byte swizzle's order), stored by one TMA box; the thread does not wait on
-                    // 32 scattered row stores
+                    pb[e] = has ? pb[e] : 0u;
+                tmem_st32(tl + COL_SPARE + 32 * x, pb);  // kept in TMEM until after this thread's next pass
+                tmem_wait_st();
+                // O is free for the next item once both threads of every row are here
+                fence_before();
+                named_bar(bar_epi, 64);
+                fence_after();
 #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        if (lane == 0)
-                            bulk_wait_read0();  // the previous box has been read out of the buffer
-                        __syncwarp();
-#pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(
-                                             stage + lane * 64 + ((c ^ ((lane >> 1) & 3)) * 16)),
-                                         "f"(__uint_as_float(o[16 * hf + 4 * c]) * inv),
-                                         "f"(__uint_as_float(o[16 * hf + 4 * c + 1]) * inv),
-                                         "f"(__uint_as_float(o[16 * hf + 4 * c + 2]) * inv),
-                                         "f"(__uint_as_float(o[16 * hf + 4 * c + 3]) * inv)
-                                         : "memory");
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == 0) {
-                            tma_store_2d(&p.to, stage, int(h * SD + 64 * x + 32 * k + 16 * hf), int(t.row0 + 32 * qd));
-                            bulk_commit();
-                        }
-                    }
-                } else if (store) {
-                    out_store32(p.o, orow + 32 * k, o, inv, p.o_type);
-                }
+                for (int e = 0; e < 32; ++e)
+                    pa[e] = has ? pa[e] : 0u;
+                store_chunk(0, pa);
             }
-            // O and the sum shares are read by both threads of the row before either starts the next item
-            fence_before();
-            named_bar(bar_epi, 64);
-            fence_after();
+            pend = 1;
             ii = ii_n;
             t = tn;
         }
+        while (pend > 0)
+            store_one();
         if (!ok && lane == 0)
             atomicExch(p.err, 13);
         if (lane == 0)
