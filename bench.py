@@ -198,7 +198,7 @@ class Prefill(Workload):
     bound = "tensor"
 
     def __init__(self, name, metric, B, H, KV, D, S, dtype, scale, block, seed, rms_qk=False, cfg="", world=1,
-                 rank=0):
+                 rank=0, sharded=False):
         import torch
         from mako_attn.shard import head_shard
         self.name, self.metric, self.unit = name, metric, "TFLOP/s"
@@ -209,7 +209,8 @@ class Prefill(Workload):
         self.heads_all, self.kv_all = B * H, B * KV
         self.world, self.rank = world, rank
         self.head0, self.heads, self.kv0, self.kv_heads = head_shard(self.heads_all, self.kv_all, world, rank)
-        self.scaling = "strong" if world > 1 else "weak"
+        # sharded: one problem at every N (its heads shared out when N > 1); else one replica per GPU
+        self.scaling = "strong" if sharded else "weak"
         self.q_pad, self.k_pad = round_up(S, 64), round_up(S, 128)
         self.q = torch.zeros((self.heads, self.q_pad, D), dtype=self.tdtype, device=DEVICE)
         self.k = torch.zeros((self.kv_heads, self.k_pad, D), dtype=self.tdtype, device=DEVICE)
@@ -337,7 +338,7 @@ class DecodeLong(Workload):
         self.world, self.rank = world, rank
         self.start, self.n = kv_shard(L, world, rank)
         self.stride = round_up(max(self.n, 1), 64)
-        self.scaling = "strong" if world > 1 else "weak"
+        self.scaling = "strong"  # one sequence at every N (its keys shared out when N > 1)
         self.q = gen_heads(0, 1, self.H, self.D, torch.float16, seed + 1)  # [1][H][D]
         self.k = torch.zeros((1, self.KV, self.stride, self.D), dtype=torch.float16, device=DEVICE)
         self.v = torch.zeros_like(self.k)
@@ -621,7 +622,7 @@ def make_workload(name, world=1, rank=0):
         return DecodeLong(world=world, rank=rank)
     if name == "prefill":
         return Prefill("prefill", "prefill attention TFLOP/s (causal GQA)", 2, 32, 8, 128, 8192, "bf16", 0.5,
-                       UINT32_MAX, 0, cfg="prefill (configs[2])", world=world, rank=rank)
+                       UINT32_MAX, 0, cfg="prefill (configs[2])", world=world, rank=rank, sharded=True)
     if name == "prefill_small":
         return Prefill("prefill_small", "prefill attention TFLOP/s (causal GQA)", 1, 16, 8, 128, 512, "fp16", 1.0,
                        UINT32_MAX, 0, cfg="prefill_small (configs[0])")
@@ -631,7 +632,7 @@ def make_workload(name, world=1, rank=0):
                        cfg="prefill_d256 (Qwen3.5 gated-attention head shape, synthetic; not a BASELINE config)")
     if name == "bidir":
         return Prefill("bidir", "bidirectional attention TFLOP/s (video DiT)", 1, 24, 24, 128, 75600, "bf16", 1.0, 0,
-                       0, rms_qk=True, cfg="bidir (configs[4])", world=world, rank=rank)
+                       0, rms_qk=True, cfg="bidir (configs[4])", world=world, rank=rank, sharded=True)
     if name == "sparse":
         return Sparse()
     if name == "heads":
