@@ -352,6 +352,56 @@ def test_block_sparse_irregular_lists(ctx, oracle, dtype):
     assert np.all(got[5 * 64:6 * 64, 3 * 128:4 * 128] == 0.0)
 
 
+def ramp_keys(k_bits, dtype, n_k, block_rows, top):
+    """K rows scaled up key block by key block (factor 1 at the first block to `top` at the last), so that a row's
+    running maximum rises by more than the lazy-rescale threshold (8 in log2 units) several times along its keys:
+    the rescale of O and, in the kernels that split a row's passes over two warpgroups, the hand-over of the maximum
+    between them are exercised."""
+    import oracle as O
+    k = O.from_bits(k_bits, dtype)
+    blocks = np.arange(k.shape[1]) // block_rows
+    last = max(1, (n_k - 1) // block_rows)
+    fac = 1.0 + (top - 1.0) * np.minimum(blocks, last) / last
+    return O.to_bits(k * fac[None, :, None].astype(np.float32), dtype)
+
+
+@pytest.mark.parametrize("dim", [128, 256])
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_dense_rising_scores(ctx, oracle, dim, dtype):
+    """Causal prefill whose scores grow along the keys (the running maximum is raised mid-row, O rescaled)."""
+    case = C.dense_case(seed=140 + dim + dtype, heads=4, kv_heads=2, dim=dim, n_q=1000, n_k=1000, dtype=dtype)
+    case["k"] = ramp_keys(case["k"], dtype, case["n_k"], 64, 10.0)
+    got = run_dense(ctx, case)
+    assert ctx.device_error() == 0
+    want = oracle_dense(oracle, case)
+    ok, stats = C.within(got[:case["n_q"]], want)
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_block_sparse_rising_scores(ctx, oracle, dtype):
+    """Block-sparse lists (ascending) over keys whose scores grow cube by cube: the running maximum handed from
+    pass to pass is raised several times within a row, and O is rescaled between the two parities' products."""
+    import torch
+    heads, n = 2, 2048
+    nb = n // 64
+    lists, counts = C.block_lists(150 + dtype, heads, nb, 0.3)
+    case = C.dense_case(seed=151 + dtype, heads=heads, kv_heads=heads, dim=128, n_q=n, n_k=n, dtype=dtype)
+    case["k"] = ramp_keys(case["k"], dtype, n, 64, 10.0)
+    q, k, v = dev(case["q"], dtype), dev(case["k"], dtype), dev(case["v"], dtype)
+    o = torch.full((n, heads * 128), SENTINEL, dtype=torch.float32, device="cuda")
+    ctx.attention_block_sparse(q, k, v, o, n, heads, heads, dev_raw(lists), dev_raw(counts))
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    got = o.cpu().numpy()
+    want = oracle.attention_sparse(dtype, case["q"], case["k"], case["v"], n, case["q_pad"], n, case["k_pad"], heads,
+                                   heads, heads * 128, nb, lists.shape[-1], n, n, lists.astype(np.uint16),
+                                   counts.astype(np.uint16), np.ones(case["k_pad"], np.uint8),
+                                   np.arange(case["q_pad"], dtype=np.int32))[:n]
+    ok, stats = C.within(got, want)
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+
+
 def h3_layout(seed, frames, ph, pw, dense, heads, kv_heads, dtype):
     """A cube layout as H3 builds it (src/models/h3.cpp:510-546), from the library's mako_cube_layout: 4x4x4 cubes
     over (frame, patch row, patch column) with partial cubes at the grid edges (their rows scattered, not leading),
