@@ -54,7 +54,11 @@ enum {
      * call's 16-bit type (the values the reference's to_half / to_bf16 pass makes of its fp32 o before the output
      * projection, src/gpu/runtime.cpp:164-190), 2 bytes per value, `o` pointing at that storage; o row widths of the
      * prefill paths a multiple of 8.  0 (default): fp32 o.  The sharded forms keep fp32 (MAKO_ENOTSUP when set). */
-    MAKO_OPT_OUTPUT_16BIT = 5
+    MAKO_OPT_OUTPUT_16BIT = 5,
+    /* The persistent kernels' grid (tcgen05 dense and block-sparse attention, the output projection): 0 (default) one
+     * CTA per SM; n > 0 at most n CTAs, each then working through more items -- for tests of the paths that carry
+     * one item's state into the next on small problems. */
+    MAKO_OPT_GRID_CTAS = 6
 };
 
 typedef struct mako_attn_ctx mako_attn_ctx;

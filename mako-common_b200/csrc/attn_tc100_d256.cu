@@ -354,9 +354,13 @@ __global__ void __launch_bounds__(WNT, 1) attn_tc256_kernel(const __grid_constan
                 fence_before();
                 mbar_arrive(p_full(b));
             }
-            // O is final once the item's last P.V has finished (pv_done completes once per key tile)
+            // O is final once the item's last P.V has finished.  pv_done completes once per key tile and a parity
+            // wait cannot tell a phase from the one two before it, so the wait goes phase by phase: P.V(nb - 3)
+            // finished before S(nb - 1) was seen, P.V(nb - 2) and P.V(nb - 1) are waited for in turn.
             if (ok && nb > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (g + nb - 1) & 1, W_WAIT_LIMIT));
+                bool w = nb < 2 || mbar_wait(pv_done, (g + nb - 2) & 1, W_WAIT_LIMIT);
+                w = w && mbar_wait(pv_done, (g + nb - 1) & 1, W_WAIT_LIMIT);
+                ok = __all_sync(0xffffffffu, w);
                 fence_after();
             }
             g += nb;

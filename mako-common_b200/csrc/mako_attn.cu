@@ -26,6 +26,9 @@ struct mako_attn_ctx {
     uint64_t launches = 0;   // kernels enqueued
     bool timing = false;     // MAKO_OPT_KERNEL_TIMING
     bool out16 = false;      // MAKO_OPT_OUTPUT_16BIT
+    int grid_ctas = 0;       // MAKO_OPT_GRID_CTAS
+    // CTAs of a persistent kernel's grid: one per SM, or fewer when MAKO_OPT_GRID_CTAS asks
+    uint32_t persistent_ctas() const { return uint32_t(grid_ctas > 0 && grid_ctas < num_sms ? grid_ctas : num_sms); }
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;  // main-kernel event pairs, [0, used) recorded
     size_t used = 0;
     struct Buf {
@@ -243,6 +246,11 @@ int mako_attn_set_option(mako_attn_ctx* ctx, int option, int64_t value)
     case MAKO_OPT_OUTPUT_16BIT:
         ctx->out16 = value != 0;
         return MAKO_OK;
+    case MAKO_OPT_GRID_CTAS:
+        if (value < 0 || value > (int64_t(1) << 20))
+            return fail(MAKO_EINVAL, "grid CTAs %lld (0: one per SM)", (long long)value);
+        ctx->grid_ctas = int(value);
+        return MAKO_OK;
     case MAKO_OPT_DECODE_CHUNK:
         if (value < 0 || value % 64 || value > (int64_t(1) << 30))
             return fail(MAKO_EINVAL, "decode chunk %lld (0 or a multiple of 64)", (long long)value);
@@ -365,7 +373,7 @@ int mako_attention(mako_attn_ctx* ctx, void* stream, int dtype, const void* q, c
         return launched("attention (decode combine)", mako::launch_decode_combine(p, int(dim), st));
     }
     mako::AttnParams p{};
-    p.num_sms = uint32_t(ctx->num_sms);
+    p.num_sms = ctx->persistent_ctas();
     p.q = q;
     p.k = k;
     p.v = v;
@@ -587,7 +595,7 @@ int mako_attention_sparse(mako_attn_ctx* ctx, void* stream, int dtype, const voi
     if (n_q == 0)
         return MAKO_OK;
     mako::AttnParams p{};
-    p.num_sms = uint32_t(ctx->num_sms);
+    p.num_sms = ctx->persistent_ctas();
     p.q = q;
     p.k = k;
     p.v = v;
@@ -624,7 +632,7 @@ int mako_attention_block_sparse(mako_attn_ctx* ctx, void* stream, int dtype, con
     if (n == 0)
         return MAKO_OK;
     mako::AttnParams p{};
-    p.num_sms = uint32_t(ctx->num_sms);
+    p.num_sms = ctx->persistent_ctas();
     p.q = q;
     p.k = k;
     p.v = v;
@@ -812,7 +820,7 @@ int mako_proj(mako_attn_ctx* ctx, void* stream, int dtype, const void* w, const 
     p.k = k;
     p.n = n;
     p.ldy = ldy;
-    p.num_sms = uint32_t(ctx->num_sms);
+    p.num_sms = ctx->persistent_ctas();
     auto st = static_cast<cudaStream_t>(stream);
     ctx->launches += 1;
     KernelTimer t(ctx, st);
@@ -1098,7 +1106,7 @@ int mako_attention_gather(mako_attn_group* g, void* stream, int dtype, const voi
         return cuda_fail("set device", dg.err);
     auto st = static_cast<cudaStream_t>(stream);
     mako::AttnParams p{};
-    p.num_sms = uint32_t(ctx->num_sms);
+    p.num_sms = ctx->persistent_ctas();
     p.q = q;
     p.k = k;
     p.v = v;

@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(HERE, "libmako_attn.so")
 
 F16, BF16 = 0, 1
 OK, EINVAL, ENOMEM, ECUDA, ENOTSUP = 0, -22, -12, -5, -95
-OPT_PREFILL_KERNEL, OPT_DECODE_ROUTE, OPT_DECODE_CHUNK, OPT_KERNEL_TIMING, OPT_OUTPUT_16BIT = 1, 2, 3, 4, 5
+OPT_PREFILL_KERNEL, OPT_DECODE_ROUTE, OPT_DECODE_CHUNK, OPT_KERNEL_TIMING, OPT_OUTPUT_16BIT, OPT_GRID_CTAS = 1, 2, 3, 4, 5, 6
 UINT32_MAX = 0xFFFFFFFF
 
 # Every symbol include/mako_attn.h declares, for the load check.

@@ -461,6 +461,51 @@ def test_sparse_h3_layout(ctx, oracle, kernel, dtype):
     assert np.all(got[L["n_out"]:] == SENTINEL)
 
 
+# The persistent kernels take one work item per CTA on the small problems above (fewer items than SMs); with the grid
+# capped at a few CTAs each CTA works through many items, so the state carried from one item to the next (barrier
+# phases, the next item's Q, the epilogue overlapping the next item's first products) is exercised too.
+FEW_CTAS = 3
+
+
+@pytest.fixture
+def few_ctas(ctx):
+    import mako_attn
+    ctx.set_option(mako_attn.OPT_GRID_CTAS, FEW_CTAS)
+    yield
+    ctx.set_option(mako_attn.OPT_GRID_CTAS, 0)
+
+
+@pytest.mark.parametrize("name,kw", [c for c in DENSE if c[0] in ("config1", "ragged-causal", "bidir-gqa", "block-mask",
+                                                                    "q-offset", "d64-gqa-long", "d256", "d256-gqa-long",
+                                                                    "d256-offset-block")],
+                         ids=lambda c: c if isinstance(c, str) else "")
+def test_dense_few_ctas(ctx, oracle, few_ctas, name, kw):
+    test_dense(ctx, oracle, name, kw, 0)
+
+
+@pytest.mark.parametrize("dim", [128, 256])
+def test_dense_rising_scores_few_ctas(ctx, oracle, few_ctas, dim):
+    test_dense_rising_scores(ctx, oracle, dim, 1)
+
+
+def test_block_sparse_few_ctas(ctx, oracle, few_ctas):
+    test_block_sparse_lists(ctx, oracle, 0)
+    test_block_sparse_rising_scores(ctx, oracle, 1)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_block_sparse_irregular_few_ctas(ctx, oracle, few_ctas, dtype):
+    test_block_sparse_irregular_lists(ctx, oracle, dtype)
+
+
+def test_sparse_h3_layout_few_ctas(ctx, oracle, few_ctas):
+    test_sparse_h3_layout(ctx, oracle, 0, 1)
+
+
+def test_sparse_reference_fixture_few_ctas(ctx, oracle, few_ctas):
+    test_sparse_reference_fixture(ctx, oracle, 0)
+
+
 def test_argument_errors(ctx):
     import torch
     import mako_attn

@@ -45,6 +45,19 @@ def test_proj_matches_oracle(ctx, oracle, T, k, n, ldy, dtype):
         assert np.all(got[:, n:] == 12345.0), "columns past n were written"
 
 
+@pytest.mark.parametrize("ctas", [1, 3])
+def test_proj_few_ctas(ctx, oracle, ctas):
+    """The persistent grid capped at a few CTAs (MAKO_OPT_GRID_CTAS): each CTA works through many output tiles,
+    alternating its two TMEM accumulators, so a tile's epilogue overlaps the next tile's products."""
+    import mako_attn
+    ctx.set_option(mako_attn.OPT_GRID_CTAS, ctas)
+    try:
+        test_proj_matches_oracle(ctx, oracle, 1000, 1024, 768, 0, 1)
+        test_proj_matches_oracle(ctx, oracle, 300, 256, 520, 0, 1)
+    finally:
+        ctx.set_option(mako_attn.OPT_GRID_CTAS, 0)
+
+
 def test_attention_then_proj(ctx, oracle):
     """The consumer as the models call it: causal attention with 16-bit output (the reference's to_bf16 of o fused into
     the epilogue), then the projection straight from it; against the oracle's attention rounded to bf16 and its
