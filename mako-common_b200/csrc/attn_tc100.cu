@@ -480,32 +480,81 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
     }
 }
 
-// ---- bf16 V -> scaled fp16 copy -----------------------------------------------------------------------------------
+// ---- bf16 V -> fp16 copy ------------------------------------------------------------------------------------------
+//
+// One read of V and one write of the copy in the common case: vconv_kernel converts every value as it is (no scale)
+// and records each kv head's max |v| over the rows that can be attended (rows < n_rows with valid[row] != 0, as float
+// bits); vfix_kernel then looks at that maximum.  A head whose maximum lies in [2^-3, 2^16) (or is 0) keeps the
+// unscaled copy: nothing overflows fp16, and a value below fp16's normal range (2^-14) is off by at most 2^-25, under
+// 2^-22 of the head's maximum.  Any other head (tiny, huge, inf or NaN) is converted again from V with the power of two
+// that puts its maximum in [2^14, 2^15) -- exact for every value above 2^-28 of the maximum -- and vinv = 2^-k undoes
+// it in the epilogue.  Rows that cannot be attended are written as zeros.
 
-// vmax[kvh] = max |v| over the rows that can be attended (rows < n_rows with valid[row] != 0), as float bits.
-__global__ void __launch_bounds__(256) vmax_kernel(const __nv_bfloat16* v, uint32_t* vmax, uint32_t dim, uint32_t k_pad,
-                                                   uint32_t n_rows, const uint8_t* valid)
+// The maxima that keep the unscaled copy: 0, or [2^-3, 2^16) as float bits.
+__device__ __forceinline__ bool v_unscaled_ok(uint32_t bits)
 {
-    const uint32_t kvh = blockIdx.y;
-    const uint4* src = reinterpret_cast<const uint4*>(v + uint64_t(kvh) * k_pad * dim);
-    const uint64_t chunks = uint64_t(n_rows) * (dim / 8);
-    uint32_t best = 0;
-    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < chunks; i += uint64_t(gridDim.x) * blockDim.x) {
-        if (valid && !valid[i / (dim / 8)])
-            continue;
-        const uint4 w = src[i];
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    return bits == 0 || (bits >= (124u << 23) && bits < (143u << 23));
+}
+
+// 8 bf16 values (one 16-byte chunk) -> 8 fp16 values scaled by s, and the chunk's max |v| as float bits.
+__device__ __forceinline__ uint4 v_chunk(const uint4 w, float s, uint32_t& best)
+{
+    const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+    uint32_t o[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            best = max(best, (words[k] & 0x7FFFu) << 16);
-            best = max(best, (words[k] >> 16 & 0x7FFFu) << 16);
+    for (int k = 0; k < 4; ++k) {
+        best = max(best, (in[k] & 0x7FFFu) << 16);
+        best = max(best, (in[k] >> 16 & 0x7FFFu) << 16);
+        const float a = __uint_as_float(in[k] << 16) * s, b = __uint_as_float(in[k] & 0xFFFF0000u) * s;
+        o[k] = pack_half2(a, b);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+constexpr int VC_UNROLL = 4;  // 16-byte chunks a thread has in flight
+
+// Grid (bx, kv_heads), 256 threads: the copy with s (1 here; the scaled redo of vfix_kernel uses the same loop) and,
+// when vmax is given, the head's max |v| by atomicMax.  cshift = log2(dim / 8): chunk i lies in row i >> cshift.
+__device__ __forceinline__ void v_copy(const __nv_bfloat16* v, __half* v16, uint32_t* vmax, float s, uint32_t kvh,
+                                       uint32_t cshift, uint32_t k_pad, uint32_t n_rows, const uint8_t* valid)
+{
+    const uint64_t per_head = uint64_t(k_pad) << cshift;
+    const uint4* src = reinterpret_cast<const uint4*>(v) + uint64_t(kvh) * per_head;
+    uint4* dst = reinterpret_cast<uint4*>(v16) + uint64_t(kvh) * per_head;
+    const uint64_t live = uint64_t(n_rows) << cshift;  // chunks of rows that may be read
+    const uint64_t step = uint64_t(gridDim.x) * blockDim.x * VC_UNROLL;
+    uint32_t best = 0;
+    for (uint64_t i0 = uint64_t(blockIdx.x) * blockDim.x * VC_UNROLL + threadIdx.x; i0 < per_head; i0 += step) {
+        uint4 w[VC_UNROLL];
+        bool use[VC_UNROLL];
+#pragma unroll
+        for (int u = 0; u < VC_UNROLL; ++u) {
+            const uint64_t i = i0 + uint64_t(u) * blockDim.x;
+            use[u] = i < live && (!valid || valid[i >> cshift]);
+            w[u] = use[u] ? __ldcs(src + i) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < VC_UNROLL; ++u) {
+            const uint64_t i = i0 + uint64_t(u) * blockDim.x;
+            if (i < per_head)
+                dst[i] = use[u] ? v_chunk(w[u], s, best) : make_uint4(0, 0, 0, 0);
         }
     }
+    if (vmax) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-        best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if ((threadIdx.x & 31) == 0 && best)
-        atomicMax(vmax + kvh, best);
+        for (int o = 16; o > 0; o >>= 1)
+            best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+        if ((threadIdx.x & 31) == 0 && best)
+            atomicMax(vmax + kvh, best);
+    }
+}
+
+__global__ void __launch_bounds__(256) vconv_kernel(const __nv_bfloat16* v, __half* v16, uint32_t* vmax,
+                                                    uint32_t cshift, uint32_t k_pad, uint32_t n_rows,
+                                                    const uint8_t* valid)
+{
+    v_copy(v, v16, vmax, 1.0f, blockIdx.y, cshift, k_pad, n_rows, valid);
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");  // vfix may be scheduled now
 }
 
 // The power of two that puts `bits` (a float's bits, |v|max) in [2^14, 2^15), and its inverse; 1 for 0 / inf / nan.
@@ -521,34 +570,23 @@ __device__ __forceinline__ void v_scale(uint32_t bits, float& s, float& inv)
     inv = __int_as_float((127 + e - 14) << 23);
 }
 
-__global__ void __launch_bounds__(256) vconv_kernel(const __nv_bfloat16* v, __half* v16, const uint32_t* vmax,
-                                                    float* vinv, uint32_t dim, uint32_t k_pad, uint32_t n_rows,
-                                                    const uint8_t* valid)
+// Grid as vconv_kernel: vinv for every head, and the scaled copy again for the heads whose maximum needs it.
+__global__ void __launch_bounds__(256) vfix_kernel(const __nv_bfloat16* v, __half* v16, const uint32_t* vmax,
+                                                   float* vinv, uint32_t cshift, uint32_t k_pad, uint32_t n_rows,
+                                                   const uint8_t* valid)
 {
-    const uint32_t kvh = blockIdx.y;
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");  // vconv_kernel's copy and maxima are visible from here on
+    const uint32_t kvh = blockIdx.y, bits = vmax[kvh];
+    if (v_unscaled_ok(bits)) {
+        if (blockIdx.x == 0 && threadIdx.x == 0)
+            vinv[kvh] = 1.0f;
+        return;
+    }
     float s, inv;
-    v_scale(vmax[kvh], s, inv);
+    v_scale(bits, s, inv);
     if (blockIdx.x == 0 && threadIdx.x == 0)
         vinv[kvh] = inv;
-    const uint4* src = reinterpret_cast<const uint4*>(v + uint64_t(kvh) * k_pad * dim);
-    uint4* dst = reinterpret_cast<uint4*>(v16 + uint64_t(kvh) * k_pad * dim);
-    const uint64_t chunks = uint64_t(k_pad) * (dim / 8);
-    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < chunks; i += uint64_t(gridDim.x) * blockDim.x) {
-        const uint32_t row = uint32_t(i / (dim / 8));
-        uint4 out = make_uint4(0, 0, 0, 0);
-        if (row < n_rows && (!valid || valid[row])) {
-            const uint4 w = src[i];
-            const uint32_t in[4] = {w.x, w.y, w.z, w.w};
-            uint32_t o[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float a = __uint_as_float(in[k] << 16) * s, b = __uint_as_float(in[k] & 0xFFFF0000u) * s;
-                o[k] = pack_half2(a, b);
-            }
-            out = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        dst[i] = out;
-    }
+    v_copy(v, v16, nullptr, s, kvh, cshift, k_pad, n_rows, valid);
 }
 
 // ---- host ----------------------------------------------------------------------------------------------------------
@@ -573,20 +611,34 @@ bool out_map(CUtensorMap* map, float* o, uint32_t n_q, uint32_t width)
 cudaError_t launch_v_to_f16(const void* v, void* v16, uint32_t* vmax, float* vinv, uint32_t dim, uint32_t kv_heads,
                             uint32_t k_pad, uint32_t n_rows, const uint8_t* valid, int num_sms, cudaStream_t st)
 {
+    if (dim != 64 && dim != 128 && dim != 256)
+        return cudaErrorInvalidValue;
     cudaError_t e = cudaMemsetAsync(vmax, 0, kv_heads * sizeof(uint32_t), st);
     if (e != cudaSuccess)
         return e;
-    const uint64_t chunks = uint64_t(k_pad) * (dim / 8);
-    uint32_t bx = uint32_t((chunks + 255) / 256);
+    const uint32_t cshift = dim == 64 ? 3 : dim == 128 ? 4 : 5;
+    const uint64_t chunks = uint64_t(k_pad) << cshift;
+    uint32_t bx = uint32_t((chunks + 256 * VC_UNROLL - 1) / (256 * VC_UNROLL));
     const uint32_t cap = uint32_t((num_sms * 8 + kv_heads - 1) / kv_heads);
     bx = bx < 1 ? 1 : (bx > cap ? cap : bx);
-    vmax_kernel<<<dim3(bx, kv_heads), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(v), vmax, dim, k_pad, n_rows,
-                                                     valid);
+    const auto* vb = static_cast<const __nv_bfloat16*>(v);
+    auto* vh = static_cast<__half*>(v16);
+    vconv_kernel<<<dim3(bx, kv_heads), 256, 0, st>>>(vb, vh, vmax, cshift, k_pad, n_rows, valid);
     if ((e = cudaGetLastError()) != cudaSuccess)
         return e;
-    vconv_kernel<<<dim3(bx, kv_heads), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(v), static_cast<__half*>(v16),
-                                                      vmax, vinv, dim, k_pad, n_rows, valid);
-    return cudaGetLastError();
+    // vfix launched as a programmatic dependent of vconv: its blocks are scheduled as vconv's last blocks run and
+    // wait (griddepcontrol.wait) for vconv's writes.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(bx, kv_heads);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, vfix_kernel, vb, vh, static_cast<const uint32_t*>(vmax), vinv, cshift, k_pad,
+                              n_rows, valid);
 }
 
 cudaError_t launch_attn_tc(const AttnParams& a, int dtype, int dim, const void* v16, const float* vinv, int* err,

@@ -52,8 +52,9 @@ cudaError_t launch_attn_tc256(const AttnParams& p, int dtype, const void* v16, c
 // walked in lockstep.  bf16 inputs need v16 / vinv (launch_v_to_f16 over all k_pad rows with the valid mask).
 cudaError_t launch_attn_tc_sparse(const AttnParams& p, int dtype, bool sel_i32, const void* v16, const float* vinv,
                                   int* err, cudaStream_t s);
-// v16 = fp16(v * 2^k) per kv head (k puts the head's max |v| over rows < n_rows with valid[row] in [2^14, 2^15);
-// other rows 0) and vinv = 2^-k, for [kv_heads][k_pad][dim] tiles.  vmax: [kv_heads] scratch.
+// v16 = fp16(v * 2^k) per kv head and vinv = 2^-k, for [kv_heads][k_pad][dim] tiles: k = 0 when the head's max |v|
+// over rows < n_rows with valid[row] lies in [2^-3, 2^16) (one read of v, one write of v16), else k puts it in
+// [2^14, 2^15) (that head converted again); other rows 0.  vmax: [kv_heads] scratch.
 cudaError_t launch_v_to_f16(const void* v, void* v16, uint32_t* vmax, float* vinv, uint32_t dim, uint32_t kv_heads,
                             uint32_t k_pad, uint32_t n_rows, const uint8_t* valid, int num_sms, cudaStream_t s);
 

@@ -402,6 +402,63 @@ def test_block_sparse_rising_scores(ctx, oracle, dtype):
     assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
 
 
+V_FACTORS = (2.0 ** -24, 2.0 ** -3, 1.0, 2.0 ** 18)  # per kv head: tiny, at the unscaled range's edge, plain, huge
+
+
+def scale_v_heads(v_bits, dtype, factors):
+    """V of kv head i multiplied by factors[i] (exact in the 16-bit type: powers of two)."""
+    import oracle as O
+    v = O.from_bits(v_bits, dtype)
+    return O.to_bits(v * np.asarray(factors, np.float32)[:, None, None], dtype)
+
+
+def per_head(o, heads, dim, kv_of, factors):
+    """o's columns of head h divided by its kv head's factor, so that one tolerance applies to every head."""
+    o = np.array(o, np.float64)
+    for h in range(heads):
+        o[..., h * dim:(h + 1) * dim] /= factors[kv_of(h)]
+    return o
+
+
+@pytest.mark.parametrize("dim", [128, 256])
+def test_bf16_v_magnitudes(ctx, oracle, dim):
+    """bf16 V whose kv heads span 2^-24 .. 2^18: the fp16 copy P.V reads keeps heads in range unscaled and
+    converts the others with a power of two, head by head; every head's output within tolerance of the oracle."""
+    heads, kvh = 8, len(V_FACTORS)
+    case = C.dense_case(seed=160 + dim, heads=heads, kv_heads=kvh, dim=dim, n_q=700, n_k=900, dtype=1)
+    case["v"] = scale_v_heads(case["v"], 1, V_FACTORS)
+    got = run_dense(ctx, case)
+    assert ctx.device_error() == 0
+    want = oracle_dense(oracle, case)
+    kv_of = lambda h: h // (heads // kvh)
+    ok, stats = C.within(per_head(got[:case["n_q"]], heads, dim, kv_of, V_FACTORS),
+                         per_head(want, heads, dim, kv_of, V_FACTORS))
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+
+
+def test_block_sparse_bf16_v_magnitudes(ctx, oracle):
+    """The block-sparse path's fp16 copy of V, heads from 2^-24 to 2^18 (see test_bf16_v_magnitudes)."""
+    import torch
+    heads, n = len(V_FACTORS), 1024
+    nb = n // 64
+    lists, counts = C.block_lists(170, heads, nb, 0.3)
+    case = C.dense_case(seed=171, heads=heads, kv_heads=heads, dim=128, n_q=n, n_k=n, dtype=1)
+    case["v"] = scale_v_heads(case["v"], 1, V_FACTORS)
+    q, k, v = dev(case["q"], 1), dev(case["k"], 1), dev(case["v"], 1)
+    o = torch.full((n, heads * 128), SENTINEL, dtype=torch.float32, device="cuda")
+    ctx.attention_block_sparse(q, k, v, o, n, heads, heads, dev_raw(lists), dev_raw(counts))
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    want = oracle.attention_sparse(1, case["q"], case["k"], case["v"], n, case["q_pad"], n, case["k_pad"], heads,
+                                   heads, heads * 128, nb, lists.shape[-1], n, n, lists.astype(np.uint16),
+                                   counts.astype(np.uint16), np.ones(case["k_pad"], np.uint8),
+                                   np.arange(case["q_pad"], dtype=np.int32))[:n]
+    kv_of = lambda h: h
+    ok, stats = C.within(per_head(o.cpu().numpy(), heads, 128, kv_of, V_FACTORS),
+                         per_head(want, heads, 128, kv_of, V_FACTORS))
+    assert ok, f"max-abs {stats[0]:.3e} rel-L2 {stats[1]:.3e} worst-row {stats[2]:.3e}"
+
+
 def h3_layout(seed, frames, ph, pw, dense, heads, kv_heads, dtype):
     """A cube layout as H3 builds it (src/models/h3.cpp:510-546), from the library's mako_cube_layout: 4x4x4 cubes
     over (frame, patch row, patch column) with partial cubes at the grid edges (their rows scattered, not leading),
