@@ -17,8 +17,9 @@ Workloads (synthetic seeded data -- no dataset is involve
   proj           the output projection after configs[2]'s attention: 16384 x 4096 bf16 o times a 4096 x 4096 bf16
                  matrix (the consumer of the attention's 16-bit output)
 A step is one call of the public C ABI (include/mako_attn.h) over one batch held in HBM; `value` is device time
-(CUDA events on the launching stream, max over ranks; L2 flushed between steps by a 256 MB write, except for an
-HBM-bound step whose inputs exceed 4x the 126 MB L2, `config.l2` says which); `e2e` is the same metric with the
+(CUDA events on the launching stream, max over ranks; L2 flushed between steps by a 256 MB write followed by a
+256 MB read, so that the step finds neither its inputs nor the flush's dirty lines in L2, except for an HBM-bound
+step whose inputs exceed 4x the 126 MB L2, `config.l2` says which); `e2e` is the same metric with the
 step's inputs copied from pinned host memory and its output read back inside the timed region.  With N > 1 the
 decode / prefill_small / prefill_d256 / sparse workloads run one replica per GPU (weak scaling); prefill and bidir
 shard the heads over the GPUs with the output all-gather fused into the attention kernel, and decode_long shards the
@@ -45,6 +46,9 @@ for p in (os.path.join(ROOT, "mako-common_b200"), os.path.join(ROOT, "oracle"), 
 UINT32_MAX = 0xFFFFFFFF
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 L2_BYTES = 126 << 20
+# The flush: a write larger than L2 evicts the previous step's lines; the read after it evicts the flush's own dirty
+# lines, whose write-back would otherwise land inside the next timed step.
+L2_FLUSH_NOTE = "flushed between steps (256 MB write, then a 256 MB read: no input and no dirty line left in L2)"
 
 
 def peaks():
@@ -63,9 +67,8 @@ def round_up(x, m):
 # ---- workloads ------------------------------------------------------------------------------------------------------
 
 def l2_flushed(W):
-    """Whether L2 is flushed (a 256 MB write) between timed steps of W, recorded in W.config["l2"]: yes, except for
-    an HBM-bound step whose inputs are more than 4x the L2 -- it cannot hit L2 across steps, and the flush's dirty
-    lines would be written back inside the next step."""
+    """Whether L2 is flushed (L2_FLUSH_NOTE) between timed steps of W, recorded in W.config["l2"]: yes, except for
+    an HBM-bound step whose inputs are more than 4x the L2 -- it cannot hit L2 across steps."""
     in_bytes = sum(t.numel() * t.element_size() for t in W.inputs)
     if W.bound == "hbm" and in_bytes >= 4 * L2_BYTES:
         W.config["l2"] = (f"not flushed: the step's inputs ({in_bytes / 1e6:.0f} MB per GPU) are more than 4x the "
@@ -157,7 +160,7 @@ class Decode(Workload):
         self.launches_per_step = 2
         self.config = {"workload": "decode (configs[1])", "batch": self.B, "q_heads": self.H, "kv_heads": self.KV,
                        "head_dim": self.D, "kv_len": [int(x) for x in self.lens], "kv_len_seed": seed,
-                       "cache_rows": self.S, "dtype": "fp16", "l2": "flushed between steps (256 MB write)"}
+                       "cache_rows": self.S, "dtype": "fp16", "l2": L2_FLUSH_NOTE}
 
     def work(self):
         return float(sum(2 * self.KV * int(L) * self.D * 2 for L in self.lens) + self.B * self.H * self.D * (2 + 4))
@@ -226,7 +229,7 @@ class Prefill(Workload):
         self.config = {"workload": cfg, "batch": B, "q_heads": H, "kv_heads": KV, "head_dim": D, "seq_len": S,
                        "mask": "causal" if block == UINT32_MAX else ("bidirectional" if block == 0 else f"block {block}"),
                        "dtype": dtype, "input_scale": scale, "rms_norm_qk": rms_qk, "seed": seed,
-                       "l2": "flushed between steps (256 MB write)"}
+                       "l2": L2_FLUSH_NOTE}
         if world > 1:
             self.config["sharding"] = (f"heads: {self.heads} q / {self.kv_heads} kv heads per rank, output slices "
                                        "stored into every rank's o by the attention kernel (fused all-gather)")
@@ -350,7 +353,7 @@ class DecodeLong(Workload):
         self.group = None
         self.config = {"workload": "decode_long (configs[1], 262144-token single-sequence variant)", "batch": 1,
                        "q_heads": self.H, "kv_heads": self.KV, "head_dim": self.D, "kv_len": L, "dtype": "fp16",
-                       "l2": "flushed between steps (256 MB write)"}
+                       "l2": L2_FLUSH_NOTE}
         if world > 1:
             self.config["sharding"] = (f"keys: {self.n} of {L} per rank; partial rows pushed to every rank over "
                                        "NVLink and merged by log-sum-exp in one kernel")
@@ -427,7 +430,7 @@ class Proj(Workload):
         self.inputs, self.outputs = [self.x, self.w], [self.y]
         self.config = {"workload": "proj (configs[2]'s output projection: 16384 tokens x 4096 -> 4096, bf16)",
                        "T": self.T, "k": self.k, "n": self.n, "dtype": "bf16", "seed": seed,
-                       "l2": "flushed between steps (256 MB write)"}
+                       "l2": L2_FLUSH_NOTE}
 
     def work(self):
         return 2.0 * self.T * self.k * self.n
@@ -489,7 +492,7 @@ class Sparse(Workload):
         self.config = {"workload": "sparse (configs[3])", "heads": self.H, "head_dim": self.D, "seq_len": self.S,
                        "block": 64, "kept_per_query_block": int(lists.shape[-1]), "keep_fraction": self.frac,
                        "mask": "int32 sorted kept-block lists + counts", "dtype": "bf16", "seed": seed,
-                       "l2": "flushed between steps (256 MB write)"}
+                       "l2": L2_FLUSH_NOTE}
 
     def work(self):
         return float(int(self.counts_np.sum()) * 4 * 64 * 64 * self.D)
@@ -560,7 +563,7 @@ class Heads(Workload):
         self.eps = 1e-6
         self.config = {"workload": "heads (configs[2] shape: batch 2, 8192 tokens, 32 q / 8 kv heads, D 128)",
                        "norm": "RMS on q and k (eps 1e-6)", "rotation": "all 128 values, halves", "tiles": "bf16",
-                       "calls_per_step": 6, "l2": "flushed between steps (256 MB write)"}
+                       "calls_per_step": 6, "l2": L2_FLUSH_NOTE}
 
     def work(self):
         B, T, H, KV, D = self.B, self.T, self.H, self.KV, self.D
@@ -770,11 +773,14 @@ def run_mako(args):
             dist.all_gather_object(out, b, group=cpu_group)
             return out
         W.setup(ctx, world, rank, exchange)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE) if l2_flushed(W) else None
+    flushing = l2_flushed(W)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE) if flushing else None
+    flush_rd = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=DEVICE) if flushing else None
 
     def flush_l2():
         if flush is not None:
             flush.zero_()
+            flush_rd.amax()
 
     stream = torch.cuda.current_stream()
 
