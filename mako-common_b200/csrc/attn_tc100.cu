@@ -35,13 +35,17 @@ using namespace tc;
 
 constexpr int TBM = 128, TBN = 128, TNS = 2, TNT = 384;
 constexpr uint32_t BOX_BYTES = 128 * 64 * 2;  // one TMA box: 128 rows x 64 16-bit values
-// Shared memory for TD-wide heads (64 or 128): Q of both tiles, the K and V rings, the barriers.
+// Shared memory for TD-wide heads (64 or 128): Q of both tiles, the K and V rings, the barriers; in the
+// head-sharded form also one output staging box (128 rows x 32 floats, 16 KB) per tile.
 template <int TD>
 struct TcSmem {
     static constexpr uint32_t TILE = (TD / 64) * BOX_BYTES;  // 128 rows x TD values
     static constexpr uint32_t Q = 0, K = 2 * TILE, V = K + TNS * TILE, BAR = V + TNS * TILE;
     static constexpr uint32_t TOTAL = BAR + 256 + 1024;  // + barriers + alignment slack
 };
+// the head-sharded form (128-wide heads): staging boxes 1024-byte aligned for the 128-byte swizzle
+constexpr uint32_t TC_STG = TcSmem<128>::BAR + 1024, TC_TOTAL_GATHER = TC_STG + 2 * BOX_BYTES + 1024;
+static_assert(TC_TOTAL_GATHER <= 227 * 1024, "the head-sharded form's shared memory");
 constexpr long long WAIT_LIMIT = 1ll << 31;             // clock cycles (~1 s) before a wait gives up
 
 struct __align__(64) TcParams {
@@ -95,10 +99,10 @@ __device__ __forceinline__ TcItem tc_item(const TcParams& p, uint32_t i)
     return it;
 }
 
-// TD: head width (64 or 128).  GATHER: the head-sharded form's epilogue (TMA stores into every rank's o, 128-wide
-// heads; launched with one item per CTA, since the epilogue stages its boxes in the Q buffer); otherwise plain
-// stores into p.od[0] and a persistent grid: while the softmax warps store one item's output, the producer already
-// loads the next item's Q and keys and the issuer starts its Q.K^T.
+// TD: head width (64 or 128).  GATHER: the head-sharded form's epilogue (TMA stores into every rank's o through a
+// staging box per tile, 128-wide heads); otherwise plain stores into p.od[0].  Either way a persistent grid: while
+// the softmax warps store one item's output, the producer already loads the next item's Q and keys and the issuer
+// starts its Q.K^T.
 template <int TD, bool GATHER>
 __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__ TcParams p)
 {
@@ -407,47 +411,40 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
             const float inv = (l > 0.0f ? 1.0f / l : 0.0f) * (p.vinv ? p.vinv[it.kvh] : 1.0f);
             const uint32_t grow = q0 + x * TBM + row;
             if (GATHER) {
-                // Head-sharded form: the tile's output goes through its Q buffer (free since its last Q.K^T) as
-                // 128-byte swizzled boxes of 128 rows x 32 floats, and TMA stores each box into every rank's o.  The
-                // stores run asynchronously -- the next CTA on this SM computes while they cross NVLink.  Two halves
-                // of 64 columns.
-                const uint32_t stage = sQ + x * TILE_BYTES;
+                // Head-sharded form: the tile's output goes through its staging box, 32 columns at a time as a
+                // 128-byte swizzled box of 128 rows x 32 floats, and TMA stores each box into every rank's o.  The
+                // stores run asynchronously: the box is rewritten once they have read it, and the next item's
+                // products run meanwhile.
+                const uint32_t stage = base + TC_STG + x * BOX_BYTES;
 #pragma unroll
-                for (int half = 0; half < TD / 64; ++half) {
+                for (int cc = 0; cc < TD / 32; ++cc) {
+                    uint32_t o[32];
+                    if (ok && nb > 0) {
+                        tmem_ld32(tl + colO + cc * 32, o);
+                        tmem_wait_ld();
+                        reg_fence(o);
+                    } else {
 #pragma unroll
-                    for (int cc = 0; cc < 2; ++cc) {
-                        uint32_t o[32];
-                        if (ok && nb > 0) {
-                            tmem_ld32(tl + colO + (2 * half + cc) * 32, o);
-                            tmem_wait_ld();
-                            reg_fence(o);
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < 32; ++e)
-                                o[e] = 0u;
-                        }
-                        const uint32_t rbase = stage + cc * BOX_BYTES + row * 128;
-#pragma unroll
-                        for (int k = 0; k < 8; ++k)
-                            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(rbase +
-                                                                                            ((k ^ (row & 7)) * 16)),
-                                         "f"(__uint_as_float(o[4 * k]) * inv), "f"(__uint_as_float(o[4 * k + 1]) * inv),
-                                         "f"(__uint_as_float(o[4 * k + 2]) * inv),
-                                         "f"(__uint_as_float(o[4 * k + 3]) * inv)
-                                         : "memory");
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = 0u;
                     }
+                    if (row == 0)
+                        bulk_wait_read0();  // the box's previous stores have read it
+                    named_bar(1 + x, 128);
+                    const uint32_t rbase = stage + row * 128;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(rbase + ((k ^ (row & 7)) * 16)),
+                                     "f"(__uint_as_float(o[4 * k]) * inv), "f"(__uint_as_float(o[4 * k + 1]) * inv),
+                                     "f"(__uint_as_float(o[4 * k + 2]) * inv), "f"(__uint_as_float(o[4 * k + 3]) * inv)
+                                     : "memory");
                     fence_proxy_async_smem();
                     named_bar(1 + x, 128);
                     if (row == 0) {
                         for (uint32_t dI = 0; dI < p.n_od; ++dI)
-#pragma unroll
-                            for (int cc = 0; cc < 2; ++cc)
-                                tma_store_2d(&p.to[dI], stage + cc * BOX_BYTES,
-                                             int((p.head0 + h) * TD + (2 * half + cc) * 32), int(q0 + x * TBM));
+                            tma_store_2d(&p.to[dI], stage, int((p.head0 + h) * TD + cc * 32), int(q0 + x * TBM));
                         bulk_commit();
-                        bulk_wait_read0();  // the staging buffer may be rewritten
                     }
-                    named_bar(1 + x, 128);
                 }
             } else {
                 const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(h) * TD;
@@ -470,6 +467,8 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
         }
         if (!ok && lane == 0)
             atomicExch(p.err, 3);
+        if (GATHER && row == 0)
+            bulk_wait0();  // the tile's last boxes have been stored
     }
     __syncwarp();
     fence_before();
@@ -695,17 +694,16 @@ cudaError_t launch_attn_tc(const AttnParams& a, int dtype, int dim, const void* 
     p.scale_log2 = a.scale * kLog2e;
     const bool gather = p.n_od > 1;
     if (gather && dim != 128)
-        return cudaErrorInvalidValue;  // the head-sharded epilogue stages 128-wide rows in the Q buffer
+        return cudaErrorInvalidValue;  // the head-sharded epilogue stages boxes of 128-wide rows
     auto kern = dim == 64 ? attn_tc_kernel<64, false> : gather ? attn_tc_kernel<128, true> : attn_tc_kernel<128, false>;
-    const uint32_t smem = dim == 64 ? TcSmem<64>::TOTAL : TcSmem<128>::TOTAL;
+    const uint32_t smem = dim == 64 ? TcSmem<64>::TOTAL : gather ? TC_TOTAL_GATHER : TcSmem<128>::TOTAL;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess)
         return e;
-    // One item per CTA for the head-sharded form (its epilogue stages in the Q buffer); otherwise one CTA per SM,
-    // each working through its share of the items.
+    // One CTA per SM, each working through its share of the items.
     const uint32_t n_items = p.n_tiles * a.heads;
     const uint32_t sms = a.num_sms ? a.num_sms : 148;
-    const uint32_t grid = gather ? n_items : (n_items < sms ? n_items : sms);
+    const uint32_t grid = n_items < sms ? n_items : sms;
     kern<<<grid, TNT, smem, st>>>(p);
     return cudaGetLastError();
 }

@@ -57,21 +57,26 @@ def set_barrier_flags(pair, epoch):
         pair.own[(par * 2 + kind) * 8 + 1] = epoch
 
 
-def test_gather_stores_the_slice_into_every_rank(ctx, oracle):
+@pytest.mark.parametrize("n,ctas", [(300, 0), (1100, 3)], ids=["one_item_per_cta", "few_ctas"])
+def test_gather_stores_the_slice_into_every_rank(ctx, oracle, n, ctas):
+    """The head-sharded kernel's output slices in both ranks' o.  few_ctas: the persistent grid capped at three CTAs
+    (MAKO_OPT_GRID_CTAS), so that each CTA stores many items' boxes through its staging buffers."""
     import torch
+    import mako_attn
     from mako_attn.shard import head_shard
-    d = C.dense_case(seed=51, heads=8, kv_heads=4, dim=128, n_q=300, n_k=300, dtype=1)
+    d = C.dense_case(seed=51, heads=8, kv_heads=4, dim=128, n_q=n, n_k=n, dtype=1)
     head0, hl, kv0, kvl = head_shard(8, 4, 2, 0)
     q = dev(d["q"][head0:head0 + hl], 1)
     k, v = dev(d["k"][kv0:kv0 + kvl], 1), dev(d["v"][kv0:kv0 + kvl], 1)
-    want = oracle.attention(1, d["q"], d["k"], d["v"], 300, d["q_pad"], 300, d["k_pad"], 8, 4, 0, C.UINT32_MAX, 128)
+    want = oracle.attention(1, d["q"], d["k"], d["v"], n, d["q_pad"], n, d["k_pad"], 8, 4, 0, C.UINT32_MAX, 128)
     pair = Pair(ctx)
+    ctx.set_option(mako_attn.OPT_GRID_CTAS, ctas)
     try:
         for _ in range(2):  # two calls: both barrier parities
-            o0 = torch.full((300, 1024), SENTINEL, dtype=torch.float32, device="cuda")
-            o1 = torch.full((300, 1024), SENTINEL, dtype=torch.float32, device="cuda")
+            o0 = torch.full((n, 1024), SENTINEL, dtype=torch.float32, device="cuda")
+            o1 = torch.full((n, 1024), SENTINEL, dtype=torch.float32, device="cuda")
             set_barrier_flags(pair, pair.next_epoch())
-            pair.g.attention_gather(q, k, v, [o0.data_ptr(), o1.data_ptr()], 300, d["q_pad"], 300, d["k_pad"], hl, kvl,
+            pair.g.attention_gather(q, k, v, [o0.data_ptr(), o1.data_ptr()], n, d["q_pad"], n, d["k_pad"], hl, kvl,
                                     head0, 1024)
             torch.cuda.synchronize()
             assert ctx.device_error() == 0
@@ -85,6 +90,7 @@ def test_gather_stores_the_slice_into_every_rank(ctx, oracle):
             par = pair.epoch & 1
             assert flags1[(par * 2) * 8 + 0] == pair.epoch and flags1[(par * 2 + 1) * 8 + 0] == pair.epoch
     finally:
+        ctx.set_option(mako_attn.OPT_GRID_CTAS, 0)
         pair.close()
 
 
