@@ -701,6 +701,19 @@ class Clocks:
                 "window": "timed region" if inside else "whole run (timed region shorter than one sample)"}
 
 
+def merge_clocks(per_rank):
+    """One clocks record from every rank's: sm_mhz the lowest per-rank median (the slowest GPU sets a step timed as
+    the max over ranks), the per-rank medians beside it, and the throttle reasons any rank saw."""
+    mhz = [c.get("sm_mhz") for c in per_rank]
+    known = [m for m in mhz if m is not None]
+    out = dict(per_rank[0])
+    out["sm_mhz"] = min(known) if known else None
+    out["per_rank_sm_mhz"] = mhz
+    out["reasons"] = sorted({r for c in per_rank for r in c.get("reasons", [])})
+    out["samples"] = sum(c.get("samples") or 0 for c in per_rank)
+    return out
+
+
 # ---- runs -----------------------------------------------------------------------------------------------------------
 
 def dist_setup():
@@ -863,6 +876,8 @@ def run_mako(args):
         ctx.set_option(mako_attn.OPT_KERNEL_TIMING, 0)
     barrier(world)
     clk = clocks.stop()
+    if world > 1:  # every GPU's clocks: the slowest one sets the step
+        clk = merge_clocks(exchange(clk))
     kernel_ms = max_over_ranks(sum(kt) / args.steps, world) if kt else None  # main kernels of one step
 
     hbm, tflops, src = peaks()

@@ -48,3 +48,18 @@ def test_reference_arm_two_ranks():
     assert lines[0]["n_gpus"] == 2
     # the device arm's rank 0 prints the same config at N = 2 (bench.arm_config), so the two lines compare
     assert lines[0]["config"]["parallelism"] == "replica x2"
+
+
+def test_clocks_of_every_rank_merge_to_the_slowest():
+    """At N > 1 the device arm's clocks record comes from every rank: the lowest per-rank median SM clock (the
+    slowest GPU sets a step timed as the max over ranks) and the throttle reasons of any rank."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    got = bench.merge_clocks([
+        {"sm_mhz": 1965, "sm_max_mhz": 1965, "reasons": ["sw_power_cap"], "samples": 30, "window": "timed region"},
+        {"sm_mhz": 1650.0, "sm_max_mhz": 1965, "reasons": [], "samples": 28, "window": "timed region"},
+    ])
+    assert got["sm_mhz"] == 1650.0 and got["per_rank_sm_mhz"] == [1965, 1650.0]
+    assert got["reasons"] == ["sw_power_cap"] and got["samples"] == 58
