@@ -16,7 +16,10 @@
 namespace mako {
 namespace {
 
-constexpr int HW = 4;  // warps (rows) a CTA
+// Warps (rows) a CTA.  One: every warp is scheduled on its own, so a slot frees the moment its row is stored and the
+// small k and v calls (1.7 waves of rows) end on a warp-sized tail rather than a CTA-sized one (0.1170 against 0.1218
+// ms for a step of config 3's six calls with 4-warp CTAs).
+constexpr int HW = 1;
 
 template <typename T>
 __device__ __forceinline__ T to16(float v);
@@ -197,7 +200,7 @@ __device__ __forceinline__ void row_out(const HeadsParams& p, int32_t t, uint32_
 }
 
 template <int VPL, typename T>
-__global__ void __launch_bounds__(HW * 32, VPL <= 4 ? 8 : 4) heads_kernel(const HeadsParams p)
+__global__ void __launch_bounds__(HW * 32, (VPL <= 4 ? 32 : 16) / HW) heads_kernel(const HeadsParams p)
 {
     __shared__ float row_buf[HW][VPL * 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
