@@ -20,7 +20,10 @@ A step is one call of the public C ABI (include/mako_attn.h) over one batch held
 (CUDA events on the launching stream, max over ranks; L2 flushed between steps by a 256 MB write followed by a
 256 MB read, so that the step finds neither its inputs nor the flush's dirty lines in L2, except for an HBM-bound
 step whose inputs exceed 4x the 126 MB L2, `config.l2` says which); `e2e` is the same metric with the
-step's inputs copied from pinned host memory and its output read back inside the timed region.  With N > 1 the
+step's inputs copied from pinned host memory and its output read back inside the timed region (on one GPU the dense
+workloads split a large step into calls over groups of heads whose copies overlap the other groups' attention;
+`e2e.pipelined` says how, and `e2e.matches_one_call_output` that the output read back equals the one-call step's
+bit for bit).  With N > 1 the
 decode / prefill_small / prefill_d256 / sparse workloads run one replica per GPU (weak scaling); prefill and bidir
 shard the heads over the GPUs with the output all-gather fused into the attention kernel, and decode_long shards the
 keys with a cross-GPU log-sum-exp combine (strong scaling: `value` is the one problem's work over the slowest rank's
@@ -274,6 +277,57 @@ class Prefill(Workload):
         else:
             self.group.attention_gather(self.q, self.k, self.v, self.obuf.ptrs, self.S, self.q_pad, self.S,
                                         self.k_pad, self.heads, self.kv_heads, self.head0, self.width, 0, self.block)
+
+    # -- the end-to-end leg at N = 1: whole GQA groups of heads, one call each, pipelined over three streams
+    E2E_GROUPS = 8              # calls a step at most
+    E2E_GROUP_BYTES = 32 << 20  # inputs a call at least: a smaller step is not worth splitting
+
+    def e2e_groups(self):
+        """(q head range, kv head range) of each call: the kv heads in up to E2E_GROUPS runs."""
+        g = self.heads // self.kv_heads
+        in_bytes = sum(t.numel() * t.element_size() for t in self.inputs)
+        n = max(1, min(self.E2E_GROUPS, self.kv_heads, in_bytes // self.E2E_GROUP_BYTES))
+        cut = [round(i * self.kv_heads / n) for i in range(n + 1)]
+        return [(a * g, b * g, a, b) for a, b in zip(cut, cut[1:]) if b > a]
+
+    def e2e_host_outputs(self):
+        """Pinned host buffers for the output, one [S][group heads * D] block per call."""
+        import torch
+        self.o_groups = [torch.empty((self.S, (h1 - h0) * self.D), dtype=torch.float32, device=DEVICE)
+                         for h0, h1, _, _ in self.e2e_groups()]
+        return [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in self.o_groups]
+
+    def e2e_note(self):
+        n = len(self.e2e_groups())
+        if n == 1:
+            return "one call a step: q, k and v copied in, attended, o read back, one after another"
+        return (f"{n} calls a step, one per group of heads: a group's q, k and v copied in on one stream, attended on "
+                "the launching stream, its o read back on a third, each waiting only for its own group's previous "
+                "stage")
+
+    def e2e_step(self, ctx, host_in, host_out, main, s_in, s_out):
+        import torch
+        hq, hk, hv = host_in
+        s_in.wait_stream(main)  # the step's start: the previous step's calls have read q, k and v
+        for (h0, h1, k0, k1), og, ho in zip(self.e2e_groups(), self.o_groups, host_out):
+            with torch.cuda.stream(s_in):
+                self.q[h0:h1].copy_(hq[h0:h1], non_blocking=True)
+                self.k[k0:k1].copy_(hk[k0:k1], non_blocking=True)
+                self.v[k0:k1].copy_(hv[k0:k1], non_blocking=True)
+            main.wait_stream(s_in)
+            ctx.attention(self.q[h0:h1], self.k[k0:k1], self.v[k0:k1], og, self.S, self.q_pad, self.S, self.k_pad,
+                          h1 - h0, k1 - k0, 0, self.block, self.D, width=(h1 - h0) * self.D, stream=main)
+            s_out.wait_stream(main)
+            with torch.cuda.stream(s_out):
+                ho.copy_(og, non_blocking=True)
+        main.wait_stream(s_out)
+
+    def e2e_matches(self, host_out):
+        """The pipelined calls' output equals the one-call step's o bit for bit (heads are independent)."""
+        import torch
+        o = self.o.cpu()
+        return all(torch.equal(ho, o[:, h0 * self.D:h1 * self.D])
+                   for (h0, h1, _, _), ho in zip(self.e2e_groups(), host_out))
 
     def sample_rows(self, n):
         import numpy as np
@@ -837,29 +891,42 @@ def run_mako(args):
     work = W.work()
     value = W.to_metric(W.total_work(world) / (ms_step / 1e3))
 
-    # end to end through the public API: pinned host inputs in, output back, every step
+    # end to end through the public API: pinned host inputs in, output back, every step.  A workload that can split
+    # its step into independent calls (the dense ones: groups of heads) pipelines them over three streams, so that
+    # one group's inputs cross PCIe while the previous group is attended and the one before it is read back.
     host_in = [t.cpu().pin_memory() for t in W.inputs]
-    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in W.outputs]
+    piped = world == 1 and hasattr(W, "e2e_groups")
+    host_out = (W.e2e_host_outputs() if piped else
+                [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in W.outputs])
     dev_in = W.inputs
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
+    s_in, s_out = (torch.cuda.Stream(), torch.cuda.Stream()) if piped else (None, None)
     e2e_times = []
     barrier(world)
     for i in range(args.warmup + args.steps):
         flush_l2()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for d, h in zip(dev_in, host_in):
-            d.copy_(h, non_blocking=True)
-        W.step(ctx)
-        for h, d in zip(host_out, W.outputs):
-            h.copy_(d, non_blocking=True)
+        if piped:
+            W.e2e_step(ctx, host_in, host_out, stream, s_in, s_out)
+        else:
+            for d, h in zip(dev_in, host_in):
+                d.copy_(h, non_blocking=True)
+            W.step(ctx)
+            for h, d in zip(host_out, W.outputs):
+                h.copy_(d, non_blocking=True)
         e1.record(stream)
         if i >= args.warmup:
             e2e_times.append((e0, e1))
     barrier(world)
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_times), world) / args.steps
     e2e_value = W.to_metric(W.total_work(world) / (e2e_ms / 1e3))
+    e2e_extra = {}
+    if piped:  # the pipelined calls' output, read back to the host, against the one-call step's o
+        torch.cuda.synchronize()
+        e2e_extra = {"pipelined": W.e2e_note(),
+                     "matches_one_call_output": bool(W.e2e_matches(host_out))}
 
     # The dominant kernel alone: the library records a CUDA event pair around each call's main kernel on the
     # launching stream (MAKO_OPT_KERNEL_TIMING), over another K steps with the same L2 handling.  A graph step holds
@@ -920,7 +987,7 @@ def run_mako(args):
             "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded normal)",
             "config": arm_config(W, world),
             "e2e": {"value": round(e2e_value, 3), "unit": W.unit, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4), **e2e_extra},
             "gpu_launches": launches, "roofline": roof, "clocks": clk, "parity": parity, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
