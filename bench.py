@@ -19,15 +19,14 @@ Workloads (synthetic seeded data -- no dataset is involve
 A step is one call of the public C ABI (include/mako_attn.h) over one batch held in HBM; `value` is device time
 (CUDA events on the launching stream, max over ranks; L2 flushed between steps by a 256 MB write followed by a
 256 MB read, so that the step finds neither its inputs nor the flush's dirty lines in L2, except for an HBM-bound
-step whose inputs exceed 4x the 126 MB L2, `config.l2` says which); `e2e` is the same metric with the
-step's inputs copied from pinned host memory and its output read back inside the timed region (on one GPU the dense
+step whose inputs exceed 4x the 126 MB L2, `config.l2` says which); `e2e` is the same metric with the step's inputs
+copied from pinned host memory and its output read back inside the timed region (on one GPU the dense and block-sparse
 workloads split a large step into calls over groups of heads whose copies overlap the other groups' attention;
-`e2e.pipelined` says how, and `e2e.matches_one_call_output` that the output read back equals the one-call step's
-bit for bit).  With N > 1 the
-decode / prefill_small / prefill_d256 / sparse workloads run one replica per GPU (weak scaling); prefill and bidir
-shard the heads over the GPUs with the output all-gather fused into the attention kernel, and decode_long shards the
-keys with a cross-GPU log-sum-exp combine (strong scaling: `value` is the one problem's work over the slowest rank's
-time).
+`e2e.pipelined` says how, and `e2e.matches_one_call_output` that the output read back equals the one-call step's bit
+for bit).  With N > 1 the decode / prefill_small / prefill_d256 / sparse workloads run one replica per GPU (weak
+scaling); prefill and bidir shard the heads over the GPUs with the output all-gather fused into the attention kernel,
+and decode_long shards the keys with a cross-GPU log-sum-exp combine (strong scaling: `value` is the one problem's
+work over the slowest rank's time).
 
 --impl reference times the reference's scalar attention restated on the CPU (oracle/, all host threads) on a
 bounded sample of the same workload: the reference itself is Metal-only and cannot run here.
@@ -553,6 +552,46 @@ class Sparse(Workload):
 
     def step(self, ctx):
         ctx.attention_block_sparse(self.q, self.k, self.v, self.o, self.S, self.H, self.H, self.lists, self.counts)
+
+    # -- the end-to-end leg at N = 1: groups of heads, one call each, pipelined over three streams (as Prefill)
+    E2E_GROUPS = 8
+
+    def e2e_groups(self):
+        cut = [round(i * self.H / self.E2E_GROUPS) for i in range(self.E2E_GROUPS + 1)]
+        return [(a, b, a, b) for a, b in zip(cut, cut[1:]) if b > a]
+
+    def e2e_host_outputs(self):
+        import torch
+        self.o_groups = [torch.empty((self.S, (h1 - h0) * self.D), dtype=torch.float32, device=DEVICE)
+                         for h0, h1, _, _ in self.e2e_groups()]
+        return [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in self.o_groups]
+
+    def e2e_note(self):
+        return (f"{len(self.e2e_groups())} calls a step, one per group of heads: a group's q, k and v copied in on one "
+                "stream, attended on the launching stream, its o read back on a third")
+
+    def e2e_step(self, ctx, host_in, host_out, main, s_in, s_out):
+        import torch
+        hq, hk, hv = host_in
+        s_in.wait_stream(main)  # the step's start: the previous step's calls have read q, k and v
+        for (h0, h1, _, _), og, ho in zip(self.e2e_groups(), self.o_groups, host_out):
+            with torch.cuda.stream(s_in):
+                self.q[h0:h1].copy_(hq[h0:h1], non_blocking=True)
+                self.k[h0:h1].copy_(hk[h0:h1], non_blocking=True)
+                self.v[h0:h1].copy_(hv[h0:h1], non_blocking=True)
+            main.wait_stream(s_in)
+            ctx.attention_block_sparse(self.q[h0:h1], self.k[h0:h1], self.v[h0:h1], og, self.S, h1 - h0, h1 - h0,
+                                       self.lists[h0:h1], self.counts[h0:h1], stream=main)
+            s_out.wait_stream(main)
+            with torch.cuda.stream(s_out):
+                ho.copy_(og, non_blocking=True)
+        main.wait_stream(s_out)
+
+    def e2e_matches(self, host_out):
+        import torch
+        o = self.o.cpu()
+        return all(torch.equal(ho, o[:, h0 * self.D:h1 * self.D])
+                   for (h0, h1, _, _), ho in zip(self.e2e_groups(), host_out))
 
     def _args(self, O):
         import numpy as np
