@@ -196,7 +196,52 @@ class Decode(Workload):
         return got, want, "sequences 0 and 7"
 
 
-class Prefill(Workload):
+class HeadGroupE2E:
+    """The end-to-end leg at N = 1 as one call per group of heads (e2e_groups: q head and kv head ranges; e2e_call:
+    the call for one group into its own [S][group heads * D] output block), pipelined over three streams: a group's
+    q, k and v are copied in on one stream, attended on the launching stream and read back on a third, so that the
+    copies of one group overlap the attention of another."""
+
+    def e2e_host_outputs(self):
+        """Pinned host buffers for the output, one block per call (and the device blocks the calls write)."""
+        import torch
+        self.o_groups = [torch.empty((self.S, (h1 - h0) * self.D), dtype=torch.float32, device=DEVICE)
+                         for h0, h1, _, _ in self.e2e_groups()]
+        return [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in self.o_groups]
+
+    def e2e_note(self):
+        n = len(self.e2e_groups())
+        if n == 1:
+            return "one call a step: q, k and v copied in, attended, o read back, one after another"
+        return (f"{n} calls a step, one per group of heads: a group's q, k and v copied in on one stream, attended on "
+                "the launching stream, its o read back on a third, each waiting only for its own group's previous "
+                "stage")
+
+    def e2e_step(self, ctx, host_in, host_out, main, s_in, s_out):
+        import torch
+        hq, hk, hv = host_in
+        s_in.wait_stream(main)  # the step's start: the previous step's calls have read q, k and v
+        for (h0, h1, k0, k1), og, ho in zip(self.e2e_groups(), self.o_groups, host_out):
+            with torch.cuda.stream(s_in):
+                self.q[h0:h1].copy_(hq[h0:h1], non_blocking=True)
+                self.k[k0:k1].copy_(hk[k0:k1], non_blocking=True)
+                self.v[k0:k1].copy_(hv[k0:k1], non_blocking=True)
+            main.wait_stream(s_in)
+            self.e2e_call(ctx, h0, h1, k0, k1, og, main)
+            s_out.wait_stream(main)
+            with torch.cuda.stream(s_out):
+                ho.copy_(og, non_blocking=True)
+        main.wait_stream(s_out)
+
+    def e2e_matches(self, host_out):
+        """The pipelined calls' output equals the one-call step's o bit for bit (heads are independent)."""
+        import torch
+        o = self.o.cpu()
+        return all(torch.equal(ho, o[:, h0 * self.D:h1 * self.D])
+                   for (h0, h1, _, _), ho in zip(self.e2e_groups(), host_out))
+
+
+class Prefill(HeadGroupE2E, Workload):
     """Dense masked prefill; batch folded into heads (head h of batch b is head b * H + h).  With N > 1 GPUs the heads
     are sharded (whole GQA groups per rank, mako_attn/shard.py) and every rank's output slice is stored into every
     rank's o by the kernel itself (mako_attention_gather): strong scaling of one problem."""
@@ -277,7 +322,7 @@ class Prefill(Workload):
             self.group.attention_gather(self.q, self.k, self.v, self.obuf.ptrs, self.S, self.q_pad, self.S,
                                         self.k_pad, self.heads, self.kv_heads, self.head0, self.width, 0, self.block)
 
-    # -- the end-to-end leg at N = 1: whole GQA groups of heads, one call each, pipelined over three streams
+    # -- the end-to-end leg at N = 1: whole GQA groups of heads, one call each (HeadGroupE2E)
     E2E_GROUPS = 8              # calls a step at most
     E2E_GROUP_BYTES = 32 << 20  # inputs a call at least: a smaller step is not worth splitting
 
@@ -289,44 +334,9 @@ class Prefill(Workload):
         cut = [round(i * self.kv_heads / n) for i in range(n + 1)]
         return [(a * g, b * g, a, b) for a, b in zip(cut, cut[1:]) if b > a]
 
-    def e2e_host_outputs(self):
-        """Pinned host buffers for the output, one [S][group heads * D] block per call."""
-        import torch
-        self.o_groups = [torch.empty((self.S, (h1 - h0) * self.D), dtype=torch.float32, device=DEVICE)
-                         for h0, h1, _, _ in self.e2e_groups()]
-        return [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in self.o_groups]
-
-    def e2e_note(self):
-        n = len(self.e2e_groups())
-        if n == 1:
-            return "one call a step: q, k and v copied in, attended, o read back, one after another"
-        return (f"{n} calls a step, one per group of heads: a group's q, k and v copied in on one stream, attended on "
-                "the launching stream, its o read back on a third, each waiting only for its own group's previous "
-                "stage")
-
-    def e2e_step(self, ctx, host_in, host_out, main, s_in, s_out):
-        import torch
-        hq, hk, hv = host_in
-        s_in.wait_stream(main)  # the step's start: the previous step's calls have read q, k and v
-        for (h0, h1, k0, k1), og, ho in zip(self.e2e_groups(), self.o_groups, host_out):
-            with torch.cuda.stream(s_in):
-                self.q[h0:h1].copy_(hq[h0:h1], non_blocking=True)
-                self.k[k0:k1].copy_(hk[k0:k1], non_blocking=True)
-                self.v[k0:k1].copy_(hv[k0:k1], non_blocking=True)
-            main.wait_stream(s_in)
-            ctx.attention(self.q[h0:h1], self.k[k0:k1], self.v[k0:k1], og, self.S, self.q_pad, self.S, self.k_pad,
-                          h1 - h0, k1 - k0, 0, self.block, self.D, width=(h1 - h0) * self.D, stream=main)
-            s_out.wait_stream(main)
-            with torch.cuda.stream(s_out):
-                ho.copy_(og, non_blocking=True)
-        main.wait_stream(s_out)
-
-    def e2e_matches(self, host_out):
-        """The pipelined calls' output equals the one-call step's o bit for bit (heads are independent)."""
-        import torch
-        o = self.o.cpu()
-        return all(torch.equal(ho, o[:, h0 * self.D:h1 * self.D])
-                   for (h0, h1, _, _), ho in zip(self.e2e_groups(), host_out))
+    def e2e_call(self, ctx, h0, h1, k0, k1, o, stream):
+        ctx.attention(self.q[h0:h1], self.k[k0:k1], self.v[k0:k1], o, self.S, self.q_pad, self.S, self.k_pad, h1 - h0,
+                      k1 - k0, 0, self.block, self.D, width=(h1 - h0) * self.D, stream=stream)
 
     def sample_rows(self, n):
         import numpy as np
@@ -524,7 +534,7 @@ class Proj(Workload):
         return float(np.sqrt(np.sum(err ** 2) / max(np.sum(np.asarray(want, np.float64) ** 2), 1e-30))) <= 1e-5
 
 
-class Sparse(Workload):
+class Sparse(HeadGroupE2E, Workload):
     name, metric, unit, bound, dtype = "sparse", "block-sparse attention TFLOP/s on kept blocks", "TFLOP/s", \
         "tensor", "bf16"
 
@@ -553,45 +563,16 @@ class Sparse(Workload):
     def step(self, ctx):
         ctx.attention_block_sparse(self.q, self.k, self.v, self.o, self.S, self.H, self.H, self.lists, self.counts)
 
-    # -- the end-to-end leg at N = 1: groups of heads, one call each, pipelined over three streams (as Prefill)
+    # -- the end-to-end leg at N = 1: groups of heads, one call each (HeadGroupE2E)
     E2E_GROUPS = 8
 
     def e2e_groups(self):
         cut = [round(i * self.H / self.E2E_GROUPS) for i in range(self.E2E_GROUPS + 1)]
         return [(a, b, a, b) for a, b in zip(cut, cut[1:]) if b > a]
 
-    def e2e_host_outputs(self):
-        import torch
-        self.o_groups = [torch.empty((self.S, (h1 - h0) * self.D), dtype=torch.float32, device=DEVICE)
-                         for h0, h1, _, _ in self.e2e_groups()]
-        return [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in self.o_groups]
-
-    def e2e_note(self):
-        return (f"{len(self.e2e_groups())} calls a step, one per group of heads: a group's q, k and v copied in on one "
-                "stream, attended on the launching stream, its o read back on a third")
-
-    def e2e_step(self, ctx, host_in, host_out, main, s_in, s_out):
-        import torch
-        hq, hk, hv = host_in
-        s_in.wait_stream(main)  # the step's start: the previous step's calls have read q, k and v
-        for (h0, h1, _, _), og, ho in zip(self.e2e_groups(), self.o_groups, host_out):
-            with torch.cuda.stream(s_in):
-                self.q[h0:h1].copy_(hq[h0:h1], non_blocking=True)
-                self.k[h0:h1].copy_(hk[h0:h1], non_blocking=True)
-                self.v[h0:h1].copy_(hv[h0:h1], non_blocking=True)
-            main.wait_stream(s_in)
-            ctx.attention_block_sparse(self.q[h0:h1], self.k[h0:h1], self.v[h0:h1], og, self.S, h1 - h0, h1 - h0,
-                                       self.lists[h0:h1], self.counts[h0:h1], stream=main)
-            s_out.wait_stream(main)
-            with torch.cuda.stream(s_out):
-                ho.copy_(og, non_blocking=True)
-        main.wait_stream(s_out)
-
-    def e2e_matches(self, host_out):
-        import torch
-        o = self.o.cpu()
-        return all(torch.equal(ho, o[:, h0 * self.D:h1 * self.D])
-                   for (h0, h1, _, _), ho in zip(self.e2e_groups(), host_out))
+    def e2e_call(self, ctx, h0, h1, k0, k1, o, stream):
+        ctx.attention_block_sparse(self.q[h0:h1], self.k[h0:h1], self.v[h0:h1], o, self.S, h1 - h0, h1 - h0,
+                                   self.lists[h0:h1], self.counts[h0:h1], stream=stream)
 
     def _args(self, O):
         import numpy as np
