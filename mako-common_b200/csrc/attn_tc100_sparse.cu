@@ -502,9 +502,10 @@ __global__ void __launch_bounds__(SNT, 1) attn_tc_sparse_kernel(const __grid_con
             auto pass = [&](auto nk_tag, uint32_t pi, uint32_t gi, uint32_t c0, uint32_t key0, uint32_t hi) {
                 constexpr int NK = decltype(nk_tag)::value;
                 uint32_t r[NK / 32][32];
-#pragma unroll
-                for (int k = 0; k < NK / 32; ++k)
-                    tmem_ld32(tl + colS + c0 + 32 * k, r[k]);
+                if constexpr (NK == 64)
+                    tmem_ld64(tl + colS + c0, r);  // the row's scores in one instruction
+                else
+                    tmem_ld128(tl + colS + c0, r);
                 tmem_wait_ld();
 #pragma unroll
                 for (int k = 0; k < NK / 32; ++k) {
