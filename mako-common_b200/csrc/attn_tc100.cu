@@ -378,8 +378,7 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                     unpack2(sum2[1], s2, s3);
                     l += (s0 + s1) + (s2 + s3);
                 }
-                tmem_st32(tl + colS, pk[0]);
-                tmem_st32(tl + colS + 32, pk[1]);
+                tmem_st64(tl + colS, pk);  // the row's P in one instruction
                 // Rescale this tile's O before P.V adds to it (PV_X(j-1) finished before S_X(j) was seen: the commit
                 // that signalled S_X(j) tracks it).
                 if (__any_sync(0xffffffffu, resc && j > 0)) {
@@ -445,22 +444,29 @@ __global__ void __launch_bounds__(TNT, 1) attn_tc_kernel(const __grid_constant__
                     }
                 }
             } else {
+                // the row's whole output read in one instruction, then stored 32 values at a time
                 const uint64_t ooff = uint64_t(grow) * p.width + uint64_t(h) * TD;
+                uint32_t o[TD / 32][32];
+                if (ok && nb > 0) {
+                    if constexpr (TD == 128)
+                        tmem_ld128(tl + colO, o);
+                    else
+                        tmem_ld64(tl + colO, o);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < TD / 32; ++c) {
-                    uint32_t o[32];
-                    if (ok && nb > 0) {
-                        tmem_ld32(tl + colO + c * 32, o);
-                        tmem_wait_ld();
-                        reg_fence(o);
-                    } else {
+                    for (int c = 0; c < TD / 32; ++c)
+                        reg_fence(o[c]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < TD / 32; ++c)
 #pragma unroll
                         for (int e = 0; e < 32; ++e)
-                            o[e] = 0u;
-                    }
-                    if (grow < p.n_q)
-                        out_store32(p.od[0], ooff + c * 32, o, inv, p.o_type);
+                            o[c][e] = 0u;
                 }
+#pragma unroll
+                for (int c = 0; c < TD / 32; ++c)
+                    if (grow < p.n_q)
+                        out_store32(p.od[0], ooff + c * 32, o[c], inv, p.o_type);
             }
         }
         if (!ok && lane == 0)
