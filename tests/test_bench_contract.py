@@ -63,3 +63,35 @@ def test_clocks_of_every_rank_merge_to_the_slowest():
     ])
     assert got["sm_mhz"] == 1650.0 and got["per_rank_sm_mhz"] == [1965, 1650.0]
     assert got["reasons"] == ["sw_power_cap"] and got["samples"] == 58
+
+
+def test_head_groups_of_the_pipelined_end_to_end_leg():
+    """The end-to-end leg's calls cover every head once, in whole GQA groups, and a small step stays one call."""
+    import importlib.util
+    import types
+    spec = importlib.util.spec_from_file_location("bench_mod2", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+
+    class T:  # the sizes e2e_groups reads from an input tensor
+        def __init__(self, n):
+            self.n = n
+
+        def numel(self):
+            return self.n
+
+        def element_size(self):
+            return 2
+
+    for heads, kv, in_elems, want_calls in ((24, 24, 3 * 24 * 75648 * 128, 8), (64, 16, 3 * 64 * 8192 * 128, 8),
+                                           (16, 8, 3 * 16 * 512 * 128, 1), (16, 2, 3 * 16 * 8192 * 256, 2)):
+        w = types.SimpleNamespace(heads=heads, kv_heads=kv, inputs=[T(in_elems)], E2E_GROUPS=8,
+                                  E2E_GROUP_BYTES=32 << 20)
+        groups = bench.Prefill.e2e_groups(w)
+        g = heads // kv
+        assert len(groups) == want_calls, (heads, kv, groups)
+        assert groups[0][0] == 0 and groups[-1][1] == heads and groups[-1][3] == kv
+        for (h0, h1, k0, k1), nxt in zip(groups, groups[1:] + [None]):
+            assert h0 == k0 * g and h1 == k1 * g and h1 > h0
+            if nxt is not None:
+                assert nxt[0] == h1 and nxt[2] == k1
