@@ -28,7 +28,7 @@ def default_plan(max_len, batch, kv_heads, heads, sms):
     rb = (group + 15) // 16
     rows = max_len * batch * kv_heads * rb
     c = -(-rows // (sms * 8))
-    c = min(max(C.round_up(c, 64), 256), 1024)
+    c = min(max(C.round_up(c, 64), 256), 2048)
     if max_len > c * 1024:
         c = -(-max_len // 1024)
     c = C.round_up(c, 64)
